@@ -1,0 +1,112 @@
+"""Sharded execution of the strided-views workload over one process per GPU.
+
+The tensor x (n0 x n1 x n2, column-major) is split along its outermost axis
+into contiguous slabs, one per rank; every rank generates or receives only its
+slab.  permute_view(x, c(3,1,2)) puts the shard axis first, so contiguous(),
+the elementwise chain and the per-element work stay local.  Two steps need the
+other ranks:
+  * global sum/var: each rank reduces its slab to (n, K, sum(x-K), sum((x-K)^2))
+    (K = first element of the slab); the rows are all-gathered and merged in
+    rank order, so the result does not depend on the collective's order;
+  * argmax along the permuted leading axis (the shard axis): each rank writes
+    one order-preserving 64-bit key per output, (ordered value bits << 32) |
+    (2^32-1 - global index) with the sign bit flipped, and a MAX all-reduce
+    picks the largest value and, among equal values, the smallest index — the
+    reference's first-index rule (src/kernels/tensor_kernels.cu:794).
+There is no peer-memory access and no multicast: the exchanged bytes are a few
+doubles and one key per output (1 MiB at 256 x 512).
+"""
+import ctypes
+from fractions import Fraction
+
+import numpy as np
+import torch
+
+from . import _lib as L
+from .tensor import _alloc, _stream, context, gpuTensor
+
+STATS_WIDTH = 6  # n, K, s1_hi, s2_hi, s1_lo, s2_lo
+
+
+# ---------------------------------------------------------------------------
+# host references of the exchange formats (also used by the CPU tests)
+# ---------------------------------------------------------------------------
+def merge_stats_exact(rows):
+    """Exact merge of per-shard rows -> (sum, var) as Python floats."""
+    n_tot = Fraction(0)
+    s1 = Fraction(0)
+    s2 = Fraction(0)
+    k0 = Fraction(rows[0][1])
+    for r in rows:
+        n, k = Fraction(r[0]), Fraction(r[1])
+        a = Fraction(r[2]) + Fraction(r[4])
+        b = Fraction(r[3]) + Fraction(r[5])
+        d = k - k0
+        s1 += a + n * d
+        s2 += b + 2 * d * a + n * d * d
+        n_tot += n
+    total = n_tot * k0 + s1
+    var = (s2 - s1 * s1 / n_tot) / (n_tot - 1) if n_tot > 1 else Fraction(0)
+    return float(total), float(var)
+
+
+def merge_stats_torch(rows):
+    """The same merge on the device in float64, rank order (rows: [G, 6])."""
+    n = rows[:, 0]
+    k = rows[:, 1]
+    a = rows[:, 2] + rows[:, 4]
+    b = rows[:, 3] + rows[:, 5]
+    d = k - k[0]
+    s1 = (a + n * d).sum()
+    s2 = (b + 2 * d * a + n * d * d).sum()
+    nt = n.sum()
+    total = nt * k[0] + s1
+    var = (s2 - s1 * (s1 / nt)) / (nt - 1)
+    return total, var
+
+
+def pack_keys_np(values, index):
+    """Host reference of the key format written by acd_argmax_keys."""
+    v = np.ascontiguousarray(values, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    ordered = np.where(v & 0x80000000, (~v) & 0xFFFFFFFF, v | 0x80000000)
+    u = (ordered << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(index, dtype=np.uint64))
+    return (u ^ np.uint64(0x8000000000000000)).view(np.int64)
+
+
+def decode_keys_np(keys, one_based=True):
+    u = np.asarray(keys, dtype=np.int64).view(np.uint64) ^ np.uint64(0x8000000000000000)
+    idx = (np.uint64(0xFFFFFFFF) - (u & np.uint64(0xFFFFFFFF))).astype(np.int64)
+    return idx + (1 if one_based else 0)
+
+
+# ---------------------------------------------------------------------------
+# device path
+# ---------------------------------------------------------------------------
+def stats_partial(x):
+    """This shard's float64[6] statistics row (device tensor)."""
+    out = torch.empty(STATS_WIDTH, dtype=torch.float64, device=x.device)
+    L.check(L.lib().acd_stats_partial(context(), ctypes.c_void_p(out.data_ptr()), ctypes.byref(x.desc()),
+                                      _stream()), "stats_partial")
+    return out
+
+
+def argmax_keys(x, axis0, index_base):
+    """Keys of the argmax along 0-based `axis0` with global index offset."""
+    kept = [x.shape[d] for d in range(x.ndims) if d != axis0]
+    n = int(np.prod(kept)) if kept else 1
+    keys = torch.empty(n, dtype=torch.int64, device=x.device)
+    L.check(L.lib().acd_argmax_keys(context(), ctypes.c_void_p(keys.data_ptr()), ctypes.byref(x.desc()), axis0,
+                                    int(index_base), _stream()), "argmax_keys")
+    return keys, kept
+
+
+def decode_keys(keys, shape, one_based=True, dtype="int32"):
+    out = _alloc(tuple(shape), dtype, keys.device)
+    L.check(L.lib().acd_argmax_keys_decode(context(), ctypes.byref(out.desc()), ctypes.c_void_p(keys.data_ptr()),
+                                           1 if one_based else 0, _stream()), "argmax_keys_decode")
+    return out
+
+
+def shard_bounds(n, rank, world):
+    """[lo, hi) of the outermost-axis slab owned by `rank`."""
+    return n * rank // world, n * (rank + 1) // world

@@ -1,0 +1,162 @@
+// Elementwise operator definitions (device).  One rounding per R operator in
+// the tensor dtype: the library is compiled with --fmad=false so no multiply
+// and add pair is contracted into an fma, and CUDA's own math functions are
+// called for exp/log/tanh/erf/sin/cos (their documented ulp bounds apply).
+//
+// Formulas follow the reference functors (src/kernels/tensor_kernels.cuh:10-192):
+// sigmoid = 1/(1+exp(-x)), relu = fmax(x, 0), round = rint (half to even),
+// max/min = fmax/fmin (NaN-ignoring), comparisons write 1 or 0.  Two
+// deliberate differences, both toward base R: x/s is a true division (the
+// reference multiplies by 1/s, src/kernels/tensor_ops.cu:1901-1913), and x^2
+// is x*x.
+#pragma once
+
+#include "common.cuh"
+
+namespace acd {
+
+__device__ __forceinline__ float m_exp(float x) { return expf(x); }
+__device__ __forceinline__ double m_exp(double x) { return exp(x); }
+__device__ __forceinline__ float m_log(float x) { return logf(x); }
+__device__ __forceinline__ double m_log(double x) { return log(x); }
+__device__ __forceinline__ float m_sqrt(float x) { return sqrtf(x); }
+__device__ __forceinline__ double m_sqrt(double x) { return sqrt(x); }
+__device__ __forceinline__ float m_erf(float x) { return erff(x); }
+__device__ __forceinline__ double m_erf(double x) { return erf(x); }
+__device__ __forceinline__ float m_tanh(float x) { return tanhf(x); }
+__device__ __forceinline__ double m_tanh(double x) { return tanh(x); }
+__device__ __forceinline__ float m_sin(float x) { return sinf(x); }
+__device__ __forceinline__ double m_sin(double x) { return sin(x); }
+__device__ __forceinline__ float m_cos(float x) { return cosf(x); }
+__device__ __forceinline__ double m_cos(double x) { return cos(x); }
+__device__ __forceinline__ float m_floor(float x) { return floorf(x); }
+__device__ __forceinline__ double m_floor(double x) { return floor(x); }
+__device__ __forceinline__ float m_ceil(float x) { return ceilf(x); }
+__device__ __forceinline__ double m_ceil(double x) { return ceil(x); }
+__device__ __forceinline__ float m_rint(float x) { return rintf(x); }
+__device__ __forceinline__ double m_rint(double x) { return rint(x); }
+__device__ __forceinline__ float m_abs(float x) { return fabsf(x); }
+__device__ __forceinline__ double m_abs(double x) { return fabs(x); }
+__device__ __forceinline__ int32_t m_abs(int32_t x) { return x < 0 ? -x : x; }
+__device__ __forceinline__ int64_t m_abs(int64_t x) { return x < 0 ? -x : x; }
+__device__ __forceinline__ float m_max(float a, float b) { return fmaxf(a, b); }
+__device__ __forceinline__ double m_max(double a, double b) { return fmax(a, b); }
+__device__ __forceinline__ int32_t m_max(int32_t a, int32_t b) { return a > b ? a : b; }
+__device__ __forceinline__ int64_t m_max(int64_t a, int64_t b) { return a > b ? a : b; }
+__device__ __forceinline__ float m_min(float a, float b) { return fminf(a, b); }
+__device__ __forceinline__ double m_min(double a, double b) { return fmin(a, b); }
+__device__ __forceinline__ int32_t m_min(int32_t a, int32_t b) { return a < b ? a : b; }
+__device__ __forceinline__ int64_t m_min(int64_t a, int64_t b) { return a < b ? a : b; }
+// float pow is evaluated in double and rounded once (CUDA's double pow is
+// within 2 ulp of double, so the float result is within 1 ulp).
+__device__ __forceinline__ float m_pow(float a, float b) { return (float)pow((double)a, (double)b); }
+__device__ __forceinline__ double m_pow(double a, double b) { return pow(a, b); }
+
+template <int OP, typename T>
+__device__ __forceinline__ T unary_apply(T x) {
+  if constexpr (OP == ACD_EXP) return m_exp(x);
+  else if constexpr (OP == ACD_LOG) return m_log(x);
+  else if constexpr (OP == ACD_SQRT) return m_sqrt(x);
+  else if constexpr (OP == ACD_ABS) return m_abs(x);
+  else if constexpr (OP == ACD_FLOOR) return m_floor(x);
+  else if constexpr (OP == ACD_CEIL) return m_ceil(x);
+  else if constexpr (OP == ACD_ROUND) return m_rint(x);
+  else if constexpr (OP == ACD_ERF) return m_erf(x);
+  else if constexpr (OP == ACD_TANH) return m_tanh(x);
+  else if constexpr (OP == ACD_SIGMOID) return T(1) / (T(1) + m_exp(-x));
+  else if constexpr (OP == ACD_RELU) return m_max(x, T(0));
+  else if constexpr (OP == ACD_SIN) return m_sin(x);
+  else if constexpr (OP == ACD_COS) return m_cos(x);
+  else if constexpr (OP == ACD_NEG) return -x;
+  else if constexpr (OP == ACD_SQUARE) return x * x;
+  else return x;  // ACD_COPY
+}
+
+template <int OP, typename T, typename O>
+__device__ __forceinline__ O binary_apply(T a, T b) {
+  if constexpr (OP == ACD_ADD) return O(a + b);
+  else if constexpr (OP == ACD_SUB) return O(a - b);
+  else if constexpr (OP == ACD_MUL) return O(a * b);
+  else if constexpr (OP == ACD_DIV) return O(a / b);
+  else if constexpr (OP == ACD_MAX) return O(m_max(a, b));
+  else if constexpr (OP == ACD_MIN) return O(m_min(a, b));
+  else if constexpr (OP == ACD_POW) return O(m_pow(a, b));
+  else if constexpr (OP == ACD_GT) return O(a > b ? 1 : 0);
+  else if constexpr (OP == ACD_LT) return O(a < b ? 1 : 0);
+  else if constexpr (OP == ACD_EQ) return O(a == b ? 1 : 0);
+  else if constexpr (OP == ACD_NE) return O(a != b ? 1 : 0);
+  else if constexpr (OP == ACD_GE) return O(a >= b ? 1 : 0);
+  else if constexpr (OP == ACD_LE) return O(a <= b ? 1 : 0);
+  else if constexpr (OP == ACD_RSUB) return O(b - a);
+  else return O(b / a);  // ACD_RDIV
+}
+
+// ---- functor objects passed to the generic kernels ------------------------
+template <int OP, typename T>
+struct UnaryF {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = T;
+  __device__ __forceinline__ T operator()(T x) const { return unary_apply<OP, T>(x); }
+};
+
+template <int OP, typename T, typename O>
+struct BinaryF {
+  static constexpr int kIn = 2;
+  using In = T;
+  using Out = O;
+  __device__ __forceinline__ O operator()(T a, T b) const { return binary_apply<OP, T, O>(a, b); }
+};
+
+template <int OP, typename T, typename O>
+struct ScalarF {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = O;
+  T s;
+  __device__ __forceinline__ O operator()(T a) const { return binary_apply<OP, T, O>(a, s); }
+};
+
+// x^2 with a scalar exponent of exactly 2 (R's `^` dispatches here).
+template <typename T>
+struct SquareScalarF {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = T;
+  __device__ __forceinline__ T operator()(T a) const { return a * a; }
+};
+
+// ---- fused chains ----------------------------------------------------------
+// x*p + exp(-(x^2)): five R operators, five roundings.
+template <typename T>
+struct FusedScaleAddExpNegSquare {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = T;
+  T p;
+  __device__ __forceinline__ T operator()(T x) const {
+    T a = x * p;
+    T sq = x * x;
+    T e = m_exp(-sq);
+    return a + e;
+  }
+};
+
+template <typename T>
+struct FusedAddRelu {
+  static constexpr int kIn = 2;
+  using In = T;
+  using Out = T;
+  __device__ __forceinline__ T operator()(T a, T b) const { return m_max(a + b, T(0)); }
+};
+
+template <typename T>
+struct FusedTanhScale {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = T;
+  T p;
+  __device__ __forceinline__ T operator()(T x) const { return m_tanh(x) * p; }
+};
+
+}  // namespace acd

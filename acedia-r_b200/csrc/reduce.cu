@@ -1,0 +1,861 @@
+// Full and per-axis reductions, arg-reductions, the fused sum+variance pass
+// and the per-shard partials used by the multi-GPU path.
+//
+// Reference counterparts and what changes:
+//   reduction_kernel + launch_reduction (src/kernels/tensor_kernels.cu:60-84,
+//   src/kernels/tensor_ops.cu:50-126): one element per thread, grid capped at
+//   65535 blocks with no grid-stride loop (only the first 16,776,960 elements
+//   are reduced), partials finished on the host.  Here: one launch over a
+//   persistent grid with 16-byte loads; the last CTA to finish merges the
+//   per-CTA partials in a fixed order, so results are deterministic and never
+//   leave the device.
+//   axis_reduction_kernel (src/kernels/tensor_kernels.cu:488-698): one block
+//   per output element, uncoalesced reads for outer axes, per-call cudaMalloc
+//   of metadata.  Here the reduced axes are collapsed to (I, R, O) and one of
+//   two layouts is used: inner (R contiguous: a warp or a CTA per output,
+//   vector loads) or outer (R strided: threads own adjacent outputs so loads
+//   along I coalesce; R is split across CTAs when I*O is small and the splits
+//   are merged in order by the last CTA of each tile).
+//   axis_variance_kernel (src/kernels/tensor_kernels.cu:810-834) writes zeros;
+//   here variance is computed for real.
+//   argmax/argmin: global argmax copies the tensor to the host
+//   (src/kernels/tensor_ops.cu:850-880), global argmin scans 256 elements
+//   (src/kernels/tensor_kernels.cu:1224-1309); both become device reductions.
+#include "common.cuh"
+#include "reduce_acc.cuh"
+
+namespace acd {
+
+template <class A>
+__device__ __forceinline__ A load_cg(const A *p) {
+  A r;
+  const int *s = reinterpret_cast<const int *>(p);
+  int *d = reinterpret_cast<int *>(&r);
+#pragma unroll
+  for (int k = 0; k < (int)(sizeof(A) / 4); ++k) d[k] = __ldcg(s + k);
+  return r;
+}
+
+constexpr int kRedThreads = 512;
+
+// Block partial -> partials[blockIdx.x]; the last CTA merges all partials in
+// index order and stores the result.  `K` re-seeds the shift of the final
+// accumulator.
+template <class Acc, typename T>
+__device__ __forceinline__ void finish_grid(Acc &acc, Acc *smem, Acc *__restrict__ partials, unsigned int *counter,
+                                            const OutSpec &os, int64_t oi, T K) {
+  __shared__ int am_last;
+  block_reduce(acc, smem);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = acc;
+    __threadfence();
+    const unsigned int t = atomicAdd(counter, 1u);
+    am_last = (t == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (am_last) {
+    __threadfence();
+    Acc f;
+    f.init();
+    if constexpr (Acc::kShift) f.set_shift(K);
+    for (int b = threadIdx.x; b < (int)gridDim.x; b += blockDim.x) f.merge(load_cg(partials + b));
+    block_reduce(f, smem);
+    if (threadIdx.x == 0) {
+      f.store(os, oi);
+      *counter = 0u;
+    }
+  }
+}
+
+// ---- full reduction over a dense range ------------------------------------
+template <class Acc, typename T, int V, int U>
+__global__ void __launch_bounds__(kRedThreads) k_red_flat(const T *__restrict__ in, int64_t n, int64_t head,
+                                                          Acc *__restrict__ partials, unsigned int *counter,
+                                                          OutSpec os) {
+  __shared__ Acc smem[kRedThreads / 32];
+  Acc acc;
+  acc.init();
+  T K = T(0);
+  if constexpr (Acc::kShift) {
+    K = in[0];
+    acc.set_shift(K);
+  }
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nvec = (n - head) / V;
+  const int64_t tail = head + nvec * V;
+  const int64_t nscalar = head + (n - tail);
+  for (int64_t i = tid; i < nscalar; i += nth) {
+    const int64_t e = i < head ? i : tail + (i - head);
+    acc.add(in[e], e);
+  }
+  const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(in + head);
+  for (int64_t v0 = tid; v0 < nvec; v0 += nth * U) {
+    Vec<T, V> x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * nth;
+      if (v < nvec) x[u] = pv[v];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t v = v0 + (int64_t)u * nth;
+      if (v < nvec) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc.add(x[u].v[k], head + v * V + k);
+      }
+    }
+  }
+  finish_grid(acc, smem, partials, counter, os, 0, K);
+}
+
+struct Space1 {
+  int32_t ndim;
+  int64_t shape[ACD_MAX_DIMS];
+  int64_t st[ACD_MAX_DIMS];
+};
+
+// ---- full reduction over any strided view (logical column-major order) ----
+template <class Acc, typename T>
+__global__ void __launch_bounds__(kRedThreads) k_red_strided(const T *__restrict__ in, Space1 g, int64_t n,
+                                                             Acc *__restrict__ partials, unsigned int *counter,
+                                                             OutSpec os) {
+  __shared__ Acc smem[kRedThreads / 32];
+  constexpr int RUN = 4;
+  Acc acc;
+  acc.init();
+  T K = T(0);
+  if constexpr (Acc::kShift) {
+    K = in[0];
+    acc.set_shift(K);
+  }
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = tid * RUN; base < n; base += nth * RUN) {
+    int64_t c[ACD_MAX_DIMS];
+    int64_t off = 0, rem = base;
+    for (int d = 0; d < g.ndim; ++d) {
+      c[d] = rem % g.shape[d];
+      rem /= g.shape[d];
+      off += c[d] * g.st[d];
+    }
+    for (int r = 0; r < RUN && base + r < n; ++r) {
+      acc.add(in[off], base + r);
+      off += g.st[0];
+      if (++c[0] == g.shape[0]) {
+        c[0] = 0;
+        off -= g.shape[0] * g.st[0];
+        for (int d = 1; d < g.ndim; ++d) {
+          off += g.st[d];
+          if (++c[d] < g.shape[d]) break;
+          c[d] = 0;
+          off -= g.shape[d] * g.st[d];
+        }
+      }
+    }
+  }
+  finish_grid(acc, smem, partials, counter, os, 0, K);
+}
+
+// ---- inner axis: out[o] = reduce_r in[o*so + r*sr], a warp per output -----
+template <class Acc, typename T, int V, bool VEC>
+__global__ void __launch_bounds__(256) k_red_inner_warp(const T *__restrict__ in, int64_t R, int64_t sr, int64_t so,
+                                                        int64_t O, OutSpec os) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t o = warp; o < O; o += nwarps) {
+    const T *p = in + o * so;
+    Acc acc;
+    acc.init();
+    if constexpr (Acc::kShift) acc.set_shift(p[0]);
+    if constexpr (VEC) {
+      constexpr int U = 4;
+      const int64_t nv = R / V;
+      const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(p);
+      for (int64_t v0 = lane; v0 < nv; v0 += 32 * U) {
+        Vec<T, V> x[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + 32 * u < nv) x[u] = pv[v0 + 32 * u];
+#pragma unroll
+        for (int u = 0; u < U; ++u)
+          if (v0 + 32 * u < nv) {
+#pragma unroll
+            for (int k = 0; k < V; ++k) acc.add(x[u].v[k], (v0 + 32 * u) * V + k);
+          }
+      }
+      for (int64_t r = nv * V + lane; r < R; r += 32) acc.add(p[r], r);
+    } else {
+      for (int64_t r = lane; r < R; r += 32) acc.add(p[r * sr], r);
+    }
+    warp_reduce(acc);
+    if (lane == 0) acc.store(os, o);
+  }
+}
+
+// ---- inner axis, few long fibers: CTAs split each fiber ---------------------
+template <class Acc, typename T, int V, bool VEC>
+__global__ void __launch_bounds__(kRedThreads) k_red_inner_cta(const T *__restrict__ in, int64_t R, int64_t sr,
+                                                               int64_t so, int64_t S, int64_t chunk,
+                                                               Acc *__restrict__ partials, unsigned int *counters,
+                                                               OutSpec os) {
+  __shared__ Acc smem[kRedThreads / 32];
+  __shared__ int am_last;
+  const int64_t o = blockIdx.x / S, s = blockIdx.x % S;
+  const T *p = in + o * so;
+  const int64_t r0 = s * chunk;
+  const int64_t r1 = (r0 + chunk < R) ? r0 + chunk : R;
+  Acc acc;
+  acc.init();
+  T K = T(0);
+  if constexpr (Acc::kShift) {
+    K = p[0];
+    acc.set_shift(K);
+  }
+  if constexpr (VEC) {  // chunk is a multiple of V, p is V-aligned
+    const int64_t v_beg = r0 / V, v_end = r1 / V;
+    const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(p);
+    constexpr int U = 4;
+    for (int64_t v0 = v_beg + threadIdx.x; v0 < v_end; v0 += (int64_t)blockDim.x * U) {
+      Vec<T, V> x[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u)
+        if (v0 + (int64_t)blockDim.x * u < v_end) x[u] = pv[v0 + (int64_t)blockDim.x * u];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int64_t v = v0 + (int64_t)blockDim.x * u;
+        if (v < v_end) {
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc.add(x[u].v[k], v * V + k);
+        }
+      }
+    }
+    for (int64_t r = v_end * V + threadIdx.x; r < r1; r += blockDim.x) acc.add(p[r], r);
+  } else {
+    for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) acc.add(p[r * sr], r);
+  }
+  block_reduce(acc, smem);
+  if (S == 1) {
+    if (threadIdx.x == 0) acc.store(os, o);
+    return;
+  }
+  if (threadIdx.x == 0) {
+    partials[o * S + s] = acc;
+    __threadfence();
+    const unsigned int t = atomicAdd(&counters[o], 1u);
+    am_last = (t == (unsigned int)(S - 1));
+  }
+  __syncthreads();
+  if (am_last && threadIdx.x == 0) {
+    __threadfence();
+    Acc f = load_cg(partials + o * S);
+    for (int64_t q = 1; q < S; ++q) f.merge(load_cg(partials + o * S + q));
+    if constexpr (Acc::kShift) f.set_shift(K);
+    f.store(os, o);
+    counters[o] = 0u;
+  }
+}
+
+// ---- outer axis: out[i + I*o] = reduce_r in[i*si + r*sr + o*so] -----------
+// A CTA covers TI = 32*V*WI consecutive i; WR warps split the r range.
+template <class Acc, typename T, int V, int WR, bool VEC>
+__global__ void __launch_bounds__(256) k_red_outer(const T *__restrict__ in, int64_t I, int64_t R, int64_t si,
+                                                   int64_t sr, int64_t so, int64_t O, int64_t S, int64_t chunk,
+                                                   int64_t itiles, Acc *__restrict__ partials,
+                                                   unsigned int *counters, OutSpec os) {
+  constexpr int WI = 8 / WR;
+  constexpr int TI = 32 * V * WI;
+  __shared__ Acc smem[WR > 1 ? WR : 1][WR > 1 ? 32 * V : 1];
+  __shared__ int am_last;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int wi = warp % WI, wr = warp / WI;
+  const int64_t s = blockIdx.x % S;
+  const int64_t rest = blockIdx.x / S;
+  const int64_t it = rest % itiles, o = rest / itiles;
+  const int64_t i0 = it * TI + (int64_t)(wi * 32 + lane) * V;
+  const int64_t r0 = s * chunk;
+  const int64_t r1 = (r0 + chunk < R) ? r0 + chunk : R;
+  const T *base = in + o * so;
+
+  Acc acc[V];
+#pragma unroll
+  for (int k = 0; k < V; ++k) {
+    acc[k].init();
+    if constexpr (Acc::kShift) {
+      if (i0 + k < I) acc[k].set_shift(base[(i0 + k) * si]);
+    }
+  }
+  const bool full = VEC && (i0 + V <= I);
+  for (int64_t r = r0 + wr; r < r1; r += WR) {
+    const T *row = base + r * sr;
+    if (full) {
+      const Vec<T, V> x = *reinterpret_cast<const Vec<T, V> *>(row + i0);
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k].add(x.v[k], r);
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (i0 + k < I) acc[k].add(row[(i0 + k) * si], r);
+    }
+  }
+  if constexpr (WR > 1) {
+    // merge the WR partial accumulators of each output in r order
+    if (wr > 0) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) smem[wr][lane * V + k] = acc[k];
+    }
+    __syncthreads();
+    if (wr == 0) {
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        for (int q = 1; q < WR; ++q) acc[k].merge(smem[q][lane * V + k]);
+    }
+  }
+  if (S == 1) {
+    if (wr == 0) {
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (i0 + k < I) acc[k].store(os, (i0 + k) + I * o);
+    }
+    return;
+  }
+  // split over r: write partials, the last CTA of this (tile, o) merges them
+  const int64_t nout = I * O;
+  if (wr == 0) {
+#pragma unroll
+    for (int k = 0; k < V; ++k)
+      if (i0 + k < I) partials[s * nout + (i0 + k) + I * o] = acc[k];
+  }
+  __threadfence();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int t = atomicAdd(&counters[it + itiles * o], 1u);
+    am_last = (t == (unsigned int)(S - 1));
+  }
+  __syncthreads();
+  if (am_last) {
+    __threadfence();
+    if (wr == 0) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) {
+        if (i0 + k < I) {
+          const int64_t oi = (i0 + k) + I * o;
+          Acc f = load_cg(partials + oi);
+          for (int64_t q = 1; q < S; ++q) f.merge(load_cg(partials + q * nout + oi));
+          if constexpr (Acc::kShift) f.set_shift(base[(i0 + k) * si]);
+          f.store(os, oi);
+        }
+      }
+    }
+    if (threadIdx.x == 0) counters[it + itiles * o] = 0u;
+  }
+}
+
+// ---- generic: any set of reduced axes, a warp per output --------------------
+struct AxisSpace {
+  int32_t nk, nr;
+  int64_t kshape[ACD_MAX_DIMS], kst[ACD_MAX_DIMS];
+  int64_t rshape[ACD_MAX_DIMS], rst[ACD_MAX_DIMS];
+};
+
+template <class Acc, typename T>
+__global__ void __launch_bounds__(256) k_red_generic(const T *__restrict__ in, AxisSpace a, int64_t O, int64_t R,
+                                                     OutSpec os) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t o = warp; o < O; o += nwarps) {
+    int64_t rem = o, base = 0;
+    for (int d = 0; d < a.nk; ++d) {
+      base += (rem % a.kshape[d]) * a.kst[d];
+      rem /= a.kshape[d];
+    }
+    Acc acc;
+    acc.init();
+    if constexpr (Acc::kShift) acc.set_shift(in[base]);
+    for (int64_t j = lane; j < R; j += 32) {
+      int64_t r = j, off = base;
+      for (int d = 0; d < a.nr; ++d) {
+        off += (r % a.rshape[d]) * a.rst[d];
+        r /= a.rshape[d];
+      }
+      acc.add(in[off], j);
+    }
+    warp_reduce(acc);
+    if (lane == 0) acc.store(os, o);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// host planning
+// ---------------------------------------------------------------------------
+struct Plan {
+  enum Kind { kFullFlat, kFullStrided, kInner, kOuter, kGeneric } kind;
+  int64_t n = 0;             // full: elements
+  const void *flat_base = nullptr;
+  Space1 sp{};
+  int64_t I = 1, R = 1, O = 1, si = 0, sr = 0, so = 0;
+  AxisSpace ax{};
+};
+
+// Builds the reduction plan for `in` with reduced-axis mask `mask`.
+static acd_status plan_reduce(const acd_desc *in, uint32_t mask, bool order_matters, Plan &p) {
+  const size_t es = dtype_size(in->dtype);
+  const char *base = desc_ptr(in);
+  int nd = 0;
+  int64_t shp[ACD_MAX_DIMS], st[ACD_MAX_DIMS];
+  bool red[ACD_MAX_DIMS];
+  for (int d = 0; d < in->ndim; ++d) {
+    if (in->shape[d] == 1) continue;
+    shp[nd] = in->shape[d];
+    st[nd] = in->stride[d];
+    red[nd] = (mask >> d) & 1u;
+    ++nd;
+  }
+  bool all = true;
+  for (int d = 0; d < nd; ++d) all = all && red[d];
+  if (all) {
+    p.n = 1;
+    for (int d = 0; d < nd; ++d) p.n *= shp[d];
+    // dense (contiguous, or a permutation of a dense block when the order of
+    // visiting does not matter): one flat range
+    bool contiguous = true;
+    int64_t expect = 1;
+    for (int d = 0; d < nd; ++d) {
+      if (st[d] != expect) contiguous = false;
+      expect *= shp[d];
+    }
+    if (contiguous || (!order_matters && is_dense_permutation(nd, shp, st))) {
+      p.kind = Plan::kFullFlat;
+      p.flat_base = base;
+      return ACD_OK;
+    }
+    p.kind = Plan::kFullStrided;
+    // collapse for the strided walk
+    IterSpace it;
+    it.ndim = nd;
+    it.nops = 1;
+    for (int d = 0; d < nd; ++d) {
+      it.shape[d] = shp[d];
+      it.stride[0][d] = st[d];
+    }
+    collapse(it);
+    p.sp.ndim = it.ndim;
+    for (int d = 0; d < ACD_MAX_DIMS; ++d) {
+      p.sp.shape[d] = d < it.ndim ? it.shape[d] : 1;
+      p.sp.st[d] = d < it.ndim ? it.stride[0][d] : 0;
+    }
+    p.flat_base = base;
+    return ACD_OK;
+  }
+  (void)es;
+  // merge neighbours with the same flag that are jointly contiguous
+  int m = 0;
+  for (int d = 0; d < nd; ++d) {
+    if (m > 0 && red[m - 1] == red[d] && st[d] == st[m - 1] * shp[m - 1]) {
+      shp[m - 1] *= shp[d];
+    } else {
+      shp[m] = shp[d];
+      st[m] = st[d];
+      red[m] = red[d];
+      ++m;
+    }
+  }
+  nd = m;
+  // (kept)? (reduced) (kept)?
+  int nruns = 0;
+  for (int d = 0; d < nd; ++d)
+    if (red[d] && (d == 0 || !red[d - 1])) ++nruns;
+  int nkept = 0;
+  for (int d = 0; d < nd; ++d) nkept += !red[d];
+  if (nruns == 1 && nd <= 3 && nkept <= 2) {
+    int r = 0;
+    while (!red[r]) ++r;
+    const bool kb = r > 0, ka = r + 1 < nd;
+    if (nd == 1 + (int)kb + (int)ka) {
+      p.I = kb ? shp[0] : 1;
+      p.si = kb ? st[0] : 0;
+      p.R = shp[r];
+      p.sr = st[r];
+      p.O = ka ? shp[r + 1] : 1;
+      p.so = ka ? st[r + 1] : 0;
+      p.flat_base = base;
+      p.kind = (p.I == 1) ? Plan::kInner : Plan::kOuter;
+      return ACD_OK;
+    }
+  }
+  p.kind = Plan::kGeneric;
+  p.ax.nk = p.ax.nr = 0;
+  p.O = p.R = 1;
+  for (int d = 0; d < nd; ++d) {
+    if (red[d]) {
+      p.ax.rshape[p.ax.nr] = shp[d];
+      p.ax.rst[p.ax.nr] = st[d];
+      p.ax.nr++;
+      p.R *= shp[d];
+    } else {
+      p.ax.kshape[p.ax.nk] = shp[d];
+      p.ax.kst[p.ax.nk] = st[d];
+      p.ax.nk++;
+      p.O *= shp[d];
+    }
+  }
+  p.flat_base = base;
+  return ACD_OK;
+}
+
+static size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+
+template <class Acc, typename T>
+static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t stream) {
+  constexpr int V = 16 / sizeof(T);
+  const T *in = static_cast<const T *>(p.flat_base);
+  switch (p.kind) {
+    case Plan::kFullFlat:
+    case Plan::kFullStrided: {
+      os.n = p.n;
+      if (p.n == 0) return fail(ACD_ERR_UNSUPPORTED, "reduction of an empty tensor");
+      int grid;
+      if (p.kind == Plan::kFullFlat)
+        grid = grid_for(ctx, (p.n + V - 1) / V, kRedThreads * 4, 2);
+      else
+        grid = grid_for(ctx, (p.n + 3) / 4, kRedThreads, 2);
+      void *scratch;
+      ACD_TRY(get_scratch(ctx, align_up(sizeof(Acc) * grid, 256), stream, &scratch));
+      Acc *partials = static_cast<Acc *>(scratch);
+      unsigned int *counter = &ctx->control->counters[0];
+      if (p.kind == Plan::kFullFlat) {
+        const int64_t c = (reinterpret_cast<uintptr_t>(in) / sizeof(T)) % V;
+        const bool al = aligned_to<T>(in, sizeof(T));
+        int64_t head = al ? (V - c) % V : p.n;
+        if (head > p.n) head = p.n;
+        k_red_flat<Acc, T, V, 4><<<grid, kRedThreads, 0, stream>>>(in, p.n, head, partials, counter, os);
+      } else {
+        k_red_strided<Acc, T><<<grid, kRedThreads, 0, stream>>>(in, p.sp, p.n, partials, counter, os);
+      }
+      return ACD_OK;
+    }
+    case Plan::kInner: {
+      os.n = p.R;
+      const bool vec = p.sr == 1 && (p.so % V == 0) && aligned_to<T>(in, sizeof(T) * V);
+      const int64_t warps_wanted = p.O;
+      const int64_t target_threads = (int64_t)ctx->sm_count * 2048;
+      if (p.O * 32 >= target_threads / 2 || p.R <= 4096) {
+        const int grid = grid_for(ctx, warps_wanted * 32, 256, 8);
+        if (vec)
+          k_red_inner_warp<Acc, T, V, true><<<grid, 256, 0, stream>>>(in, p.R, p.sr, p.so, p.O, os);
+        else
+          k_red_inner_warp<Acc, T, V, false><<<grid, 256, 0, stream>>>(in, p.R, p.sr, p.so, p.O, os);
+        return ACD_OK;
+      }
+      // few long fibers: split each over S CTAs
+      int64_t S = (target_threads / kRedThreads + p.O - 1) / p.O;
+      int64_t chunk = (p.R + S - 1) / S;
+      chunk = (chunk + 4 * V - 1) / (4 * V) * (4 * V);
+      S = (p.R + chunk - 1) / chunk;
+      void *scratch;
+      const size_t cbytes = align_up(sizeof(unsigned int) * p.O, 256);
+      ACD_TRY(get_scratch(ctx, cbytes + sizeof(Acc) * p.O * S, stream, &scratch));
+      unsigned int *counters = static_cast<unsigned int *>(scratch);
+      Acc *partials = reinterpret_cast<Acc *>(static_cast<char *>(scratch) + cbytes);
+      const int64_t grid = p.O * S;
+      if (grid > INT32_MAX) return fail(ACD_ERR_UNSUPPORTED, "reduction grid too large");
+      if (vec)
+        k_red_inner_cta<Acc, T, V, true><<<(int)grid, kRedThreads, 0, stream>>>(in, p.R, p.sr, p.so, S, chunk,
+                                                                               partials, counters, os);
+      else
+        k_red_inner_cta<Acc, T, V, false><<<(int)grid, kRedThreads, 0, stream>>>(in, p.R, p.sr, p.so, S, chunk,
+                                                                                partials, counters, os);
+      return ACD_OK;
+    }
+    case Plan::kOuter: {
+      os.n = p.R;
+      const bool vec = p.si == 1 && (p.sr % V == 0) && (p.so % V == 0) && aligned_to<T>(in, sizeof(T) * V);
+      const bool tall = p.R >= 64;
+      const int WI = tall ? 1 : 8;
+      const int64_t TI = (int64_t)32 * V * WI;
+      const int64_t itiles = (p.I + TI - 1) / TI;
+      const int64_t ctas = itiles * p.O;
+      const int64_t target_ctas = (int64_t)ctx->sm_count * 8;
+      int64_t S = 1;
+      if (tall && ctas < target_ctas) S = (target_ctas + ctas - 1) / ctas;
+      const int WR = tall ? 8 : 1;
+      int64_t chunk = (p.R + S - 1) / S;
+      chunk = (chunk + WR - 1) / WR * WR;
+      if (chunk < 8 * WR) chunk = 8 * WR;
+      S = (p.R + chunk - 1) / chunk;
+      const int64_t grid = ctas * S;
+      if (grid > INT32_MAX) return fail(ACD_ERR_UNSUPPORTED, "reduction grid too large");
+      Acc *partials = nullptr;
+      unsigned int *counters = nullptr;
+      if (S > 1) {
+        void *scratch;
+        const size_t cbytes = align_up(sizeof(unsigned int) * ctas, 256);
+        ACD_TRY(get_scratch(ctx, cbytes + sizeof(Acc) * p.I * p.O * S, stream, &scratch));
+        counters = static_cast<unsigned int *>(scratch);
+        partials = reinterpret_cast<Acc *>(static_cast<char *>(scratch) + cbytes);
+      }
+#define ACD_OUTER(WRV, VECV)                                                                            \
+  k_red_outer<Acc, T, V, WRV, VECV><<<(int)grid, 256, 0, stream>>>(in, p.I, p.R, p.si, p.sr, p.so, p.O, S, \
+                                                                   chunk, itiles, partials, counters, os)
+      if (tall) {
+        if (vec) ACD_OUTER(8, true); else ACD_OUTER(8, false);
+      } else {
+        if (vec) ACD_OUTER(1, true); else ACD_OUTER(1, false);
+      }
+#undef ACD_OUTER
+      return ACD_OK;
+    }
+    case Plan::kGeneric: {
+      os.n = p.R;
+      const int grid = grid_for(ctx, p.O * 32, 256, 8);
+      k_red_generic<Acc, T><<<grid, 256, 0, stream>>>(in, p.ax, p.O, p.R, os);
+      return ACD_OK;
+    }
+  }
+  return fail(ACD_ERR_INVALID, "bad reduction plan");
+}
+
+template <typename T>
+static acd_status reduce_t(acd_ctx *ctx, int op, const Plan &p, const OutSpec &os, cudaStream_t s) {
+  constexpr bool fl = std::is_floating_point<T>::value;
+  switch (op) {
+    case ACD_RED_SUM:
+    case ACD_RED_MEAN: return run_plan<SumAcc<T>, T>(ctx, p, os, s);
+    case ACD_RED_MAX: return run_plan<ExtAcc<T, true>, T>(ctx, p, os, s);
+    case ACD_RED_MIN: return run_plan<ExtAcc<T, false>, T>(ctx, p, os, s);
+    case ACD_RED_COUNT: return run_plan<CountAcc<T>, T>(ctx, p, os, s);
+    case ACD_RED_PROD:
+      if constexpr (fl) return run_plan<ProdAcc<T>, T>(ctx, p, os, s);
+      break;
+    case ACD_RED_VAR:
+      if constexpr (fl) return run_plan<VarAcc<T>, T>(ctx, p, os, s);
+      break;
+    default: break;
+  }
+  return fail(ACD_ERR_UNSUPPORTED, "reduction op %d not supported for this dtype", op);
+}
+
+template <typename T>
+static acd_status arg_t(acd_ctx *ctx, int op, const Plan &p, const OutSpec &os, cudaStream_t s) {
+  if (op == ACD_ARGMAX) return run_plan<ArgAcc<T, true>, T>(ctx, p, os, s);
+  return run_plan<ArgAcc<T, false>, T>(ctx, p, os, s);
+}
+
+static acd_status check_out_count(const acd_desc *out, int64_t want, const char *what) {
+  if (desc_numel(out) != want)
+    return fail(ACD_ERR_SHAPE, "%s: output has %lld elements, expected %lld", what, (long long)desc_numel(out),
+                (long long)want);
+  if (!desc_is_contiguous(out)) return fail(ACD_ERR_UNSUPPORTED, "%s: output must be contiguous", what);
+  if (out->dtype == ACD_BOOL) return fail(ACD_ERR_DTYPE, "%s: bool output not supported", what);
+  return ACD_OK;
+}
+
+static int64_t kept_count(const acd_desc *in, uint32_t mask) {
+  int64_t n = 1;
+  for (int d = 0; d < in->ndim; ++d)
+    if (!((mask >> d) & 1u)) n *= in->shape[d];
+  return n;
+}
+
+__global__ void __launch_bounds__(256) k_keys_decode(void *out, int32_t dt, const long long *__restrict__ keys,
+                                                     int64_t n, int32_t one_based) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (int64_t)gridDim.x * blockDim.x) {
+    const long long k = keys[i];
+    long long idx = -1;
+    if (k != LLONG_MIN) {
+      const uint64_t u = (uint64_t)k ^ 0x8000000000000000ull;
+      idx = (long long)(0xFFFFFFFFull - (u & 0xFFFFFFFFull)) + one_based;
+    }
+    store_i(out, dt, i, idx);
+  }
+}
+
+template <typename T>
+acd_status softmax_stats(acd_ctx *ctx, const acd_desc *in, cudaStream_t s) {
+  Plan p;
+  ACD_TRY(plan_reduce(in, 0xFFu, false, p));
+  OutSpec os;
+  os.out = ctx->control->stats;
+  os.mode = kModeValue;
+  return run_plan<SoftStatAcc<T>, T>(ctx, p, os, s);
+}
+template acd_status softmax_stats<float>(acd_ctx *, const acd_desc *, cudaStream_t);
+template acd_status softmax_stats<double>(acd_ctx *, const acd_desc *, cudaStream_t);
+
+}  // namespace acd
+
+using namespace acd;
+
+extern "C" {
+
+acd_status acd_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, uint32_t axes_mask,
+                      acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_reduce: null context");
+  ACD_TRY(check_desc(out, "out"));
+  ACD_TRY(check_desc(in, "in"));
+  if (op < ACD_RED_SUM || op > ACD_RED_COUNT) return fail(ACD_ERR_INVALID, "acd_reduce: bad op %d", op);
+  if (in->ndim < 32 && (axes_mask >> in->ndim) != 0u) return fail(ACD_ERR_AXIS, "acd_reduce: axis outside the tensor");
+  if (in->ndim == 0) axes_mask = 0;
+  ACD_TRY(check_out_count(out, kept_count(in, axes_mask), "acd_reduce"));
+  if (desc_numel(in) == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_reduce: empty input");
+  Plan p;
+  ACD_TRY(plan_reduce(in, axes_mask, false, p));
+  OutSpec os;
+  os.out = desc_ptr(out);
+  os.dt = out->dtype;
+  os.op = op;
+  os.mode = kModeValue;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  switch (in->dtype) {
+    case ACD_FLOAT32: st = reduce_t<float>(ctx, op, p, os, s); break;
+    case ACD_FLOAT64: st = reduce_t<double>(ctx, op, p, os, s); break;
+    case ACD_INT32: st = reduce_t<int32_t>(ctx, op, p, os, s); break;
+    case ACD_INT64: st = reduce_t<int64_t>(ctx, op, p, os, s); break;
+    case ACD_BOOL: st = reduce_t<uint8_t>(ctx, op, p, os, s); break;
+    default: return fail(ACD_ERR_DTYPE, "acd_reduce: bad dtype");
+  }
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_sum_var(acd_ctx *ctx, const acd_desc *out_sum, const acd_desc *out_var, const acd_desc *in,
+                       acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_sum_var: null context");
+  ACD_TRY(check_desc(in, "in"));
+  if (!out_sum && !out_var) return fail(ACD_ERR_INVALID, "acd_sum_var: no output");
+  if (out_sum) {
+    ACD_TRY(check_desc(out_sum, "out_sum"));
+    ACD_TRY(check_out_count(out_sum, 1, "acd_sum_var"));
+  }
+  if (out_var) {
+    ACD_TRY(check_desc(out_var, "out_var"));
+    ACD_TRY(check_out_count(out_var, 1, "acd_sum_var"));
+  }
+  if (!is_float(in->dtype)) return fail(ACD_ERR_DTYPE, "acd_sum_var: float32/float64 input required");
+  if (desc_numel(in) == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_sum_var: empty input");
+  Plan p;
+  ACD_TRY(plan_reduce(in, 0xFFu, false, p));
+  OutSpec os;
+  os.mode = kModeSumVar;
+  os.out = out_sum ? desc_ptr(out_sum) : nullptr;
+  os.dt = out_sum ? out_sum->dtype : ACD_FLOAT64;
+  os.out2 = out_var ? desc_ptr(out_var) : nullptr;
+  os.dt2 = out_var ? out_var->dtype : ACD_FLOAT64;
+  os.op = ACD_RED_VAR;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st = in->dtype == ACD_FLOAT32 ? run_plan<VarAcc<float>, float>(ctx, p, os, s)
+                                           : run_plan<VarAcc<double>, double>(ctx, p, os, s);
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_stats_partial(acd_ctx *ctx, double *stats, const acd_desc *in, acd_stream stream) {
+  if (!ctx || !stats) return fail(ACD_ERR_INVALID, "acd_stats_partial: null argument");
+  ACD_TRY(check_desc(in, "in"));
+  if (!is_float(in->dtype)) return fail(ACD_ERR_DTYPE, "acd_stats_partial: float32/float64 input required");
+  if (desc_numel(in) == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_stats_partial: empty input");
+  Plan p;
+  ACD_TRY(plan_reduce(in, 0xFFu, false, p));
+  OutSpec os;
+  os.mode = kModeStats;
+  os.out = stats;
+  os.op = ACD_RED_VAR;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st = in->dtype == ACD_FLOAT32 ? run_plan<VarAcc<float>, float>(ctx, p, os, s)
+                                           : run_plan<VarAcc<double>, double>(ctx, p, os, s);
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_arg_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out_index, const acd_desc *out_value,
+                          const acd_desc *in, int32_t axis, int32_t one_based, acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_arg_reduce: null context");
+  ACD_TRY(check_desc(out_index, "out_index"));
+  ACD_TRY(check_desc(in, "in"));
+  if (op != ACD_ARGMAX && op != ACD_ARGMIN) return fail(ACD_ERR_INVALID, "acd_arg_reduce: bad op %d", op);
+  if (out_index->dtype != ACD_INT32 && out_index->dtype != ACD_INT64 && out_index->dtype != ACD_FLOAT64)
+    return fail(ACD_ERR_DTYPE, "acd_arg_reduce: index output must be int32, int64 or float64");
+  if (axis >= in->ndim && !(axis == 0 && in->ndim == 0)) return fail(ACD_ERR_AXIS, "acd_arg_reduce: axis %d out of range", axis);
+  const uint32_t mask = axis < 0 ? 0xFFu : (1u << axis);
+  const int64_t kept = axis < 0 ? 1 : kept_count(in, mask);
+  ACD_TRY(check_out_count(out_index, kept, "acd_arg_reduce"));
+  if (out_value) {
+    ACD_TRY(check_desc(out_value, "out_value"));
+    ACD_TRY(check_out_count(out_value, kept, "acd_arg_reduce"));
+  }
+  if (desc_numel(in) == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_arg_reduce: empty input");
+  Plan p;
+  ACD_TRY(plan_reduce(in, mask, true, p));
+  OutSpec os;
+  os.mode = kModeIndex;
+  os.out = desc_ptr(out_index);
+  os.dt = out_index->dtype;
+  os.out2 = out_value ? desc_ptr(out_value) : nullptr;
+  os.dt2 = out_value ? out_value->dtype : ACD_FLOAT64;
+  os.one_based = one_based ? 1 : 0;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  switch (in->dtype) {
+    case ACD_FLOAT32: st = arg_t<float>(ctx, op, p, os, s); break;
+    case ACD_FLOAT64: st = arg_t<double>(ctx, op, p, os, s); break;
+    case ACD_INT32: st = arg_t<int32_t>(ctx, op, p, os, s); break;
+    case ACD_INT64: st = arg_t<int64_t>(ctx, op, p, os, s); break;
+    default: return fail(ACD_ERR_DTYPE, "acd_arg_reduce: dtype not supported");
+  }
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_argmax_keys(acd_ctx *ctx, int64_t *keys, const acd_desc *in, int32_t axis, int64_t index_base,
+                           acd_stream stream) {
+  if (!ctx || !keys) return fail(ACD_ERR_INVALID, "acd_argmax_keys: null argument");
+  ACD_TRY(check_desc(in, "in"));
+  if (in->dtype != ACD_FLOAT32) return fail(ACD_ERR_DTYPE, "acd_argmax_keys: float32 input required");
+  if (axis < 0 || axis >= in->ndim) return fail(ACD_ERR_AXIS, "acd_argmax_keys: axis %d out of range", axis);
+  if (desc_numel(in) == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_argmax_keys: empty input");
+  if (index_base < 0 || index_base + in->shape[axis] > 0xFFFFFFFFLL)
+    return fail(ACD_ERR_INVALID, "acd_argmax_keys: global index must fit in 32 bits");
+  Plan p;
+  ACD_TRY(plan_reduce(in, 1u << axis, true, p));
+  OutSpec os;
+  os.mode = kModeKey;
+  os.out = keys;
+  os.index_base = index_base;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st = run_plan<ArgAcc<float, true>, float>(ctx, p, os, s);
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const int64_t *keys, int32_t one_based,
+                                  acd_stream stream) {
+  if (!ctx || !keys) return fail(ACD_ERR_INVALID, "acd_argmax_keys_decode: null argument");
+  ACD_TRY(check_desc(out_index, "out_index"));
+  if (!desc_is_contiguous(out_index)) return fail(ACD_ERR_UNSUPPORTED, "acd_argmax_keys_decode: contiguous output required");
+  if (out_index->dtype != ACD_INT32 && out_index->dtype != ACD_INT64)
+    return fail(ACD_ERR_DTYPE, "acd_argmax_keys_decode: int32 or int64 output required");
+  const int64_t n = desc_numel(out_index);
+  if (n == 0) return ACD_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(ctx, n, 256, 4);
+  k_keys_decode<<<grid, 256, 0, s>>>(desc_ptr(out_index), out_index->dtype, reinterpret_cast<const long long *>(keys),
+                                     n, one_based ? 1 : 0);
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,343 @@
+// Cumulative sum / product along an axis, or over the column-major flattened
+// tensor.
+//
+// Reference: cumsum.gpuTensor / cumprod.gpuTensor (R/gpuTensor.R:2234-2277)
+// copy the whole tensor to the host and run base R's cumsum over the
+// flattened vector.  Here a single-pass chained scan (decoupled look-back,
+// Merrill & Garland 2016) runs on the device:
+//   * the problem is (L lanes, R steps, O outer): element (l, r, o) at
+//     l*sl + r*sr + o*so; each (lane block, o) pair is one chain of tiles
+//     along r;
+//   * CTAs take tiles from an atomic ticket, so every tile a CTA waits for
+//     was started earlier (no deadlock whatever the residency);
+//   * a tile publishes its aggregate, looks back over its predecessors'
+//     aggregates until it finds an inclusive prefix, then publishes its own
+//     inclusive prefix; flags carry the launch epoch so stale flags from
+//     earlier launches never match and the state needs no clearing;
+//   * every wait is bounded (globaltimer): on expiry the tile raises the
+//     context status word, marks the launch aborted (later waiters give up
+//     at once) and publishes anyway, so the kernel always terminates.
+// Accumulation is float64 (a float64 sum per lane; R accumulates in long
+// double and rounds each output once).
+#include "common.cuh"
+
+namespace acd {
+
+constexpr uint32_t kFlagAgg = 1u, kFlagIncl = 2u;
+
+struct ScanArgs {
+  const void *in;
+  void *out;
+  int64_t L, R, O;
+  int64_t sl, sr, so;  // input strides
+  int64_t ol, orr, oo; // output strides
+  int64_t lblocks;     // lane blocks per o
+  int64_t rtiles;      // step tiles per chain
+  int64_t ntiles;
+  uint32_t *flags;     // [ntiles]
+  double *agg;         // [ntiles][LT]
+  double *incl;        // [ntiles][LT]
+  Control *control;
+  uint32_t epoch;
+  int64_t fault_tile;
+  int64_t timeout_ns;
+};
+
+template <bool PROD>
+__device__ __forceinline__ double combine(double a, double b) {
+  return PROD ? a * b : a + b;
+}
+
+__device__ __forceinline__ uint32_t load_flag(const uint32_t *p) {
+  return *reinterpret_cast<const volatile uint32_t *>(p);
+}
+
+// Thread layout: LT lanes x G step groups (LT * G == 256).  Each thread scans
+// SEG consecutive steps of one lane in registers.
+template <typename T, bool PROD, int LT, int SEG>
+__global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
+  constexpr int G = 256 / LT;
+  constexpr int RT = G * SEG;  // steps per tile
+  __shared__ int64_t s_tile;
+  __shared__ double s_tot[G][LT];
+  __shared__ double s_prefix[LT];
+  const double ident = PROD ? 1.0 : 0.0;
+
+  if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(&a.control->counters[1], 1u);
+  __syncthreads();
+  const int64_t tile = s_tile;
+  const int64_t chain = tile / a.rtiles, q = tile % a.rtiles;
+  const int64_t o = chain / a.lblocks, lb = chain % a.lblocks;
+  const int lane = (LT == 1) ? 0 : (int)(threadIdx.x % LT);
+  const int grp = (LT == 1) ? (int)threadIdx.x : (int)(threadIdx.x / LT);
+  const int64_t l = lb * LT + lane;
+  const bool lane_ok = l < a.L;
+  const int64_t r0 = q * RT + (int64_t)grp * SEG;
+
+  const T *in = static_cast<const T *>(a.in) + o * a.so + (lane_ok ? l : 0) * a.sl;
+  T *out = static_cast<T *>(a.out) + o * a.oo + (lane_ok ? l : 0) * a.ol;
+
+  // 1. load and scan this thread's segment
+  double v[SEG];
+  double run = ident;
+#pragma unroll
+  for (int k = 0; k < SEG; ++k) {
+    const int64_t r = r0 + k;
+    double x = ident;
+    if (lane_ok && r < a.R) x = (double)in[r * a.sr];
+    run = combine<PROD>(run, x);
+    v[k] = run;
+  }
+
+  // 2. exclusive prefix of the segment totals within the tile, per lane
+  double excl = ident;
+  double tile_total = ident;
+  if constexpr (LT == 1) {
+    // block scan over 256 segment totals: warp shuffles, then warp totals
+    const int wl = threadIdx.x & 31, w = threadIdx.x >> 5;
+    double x = run;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, x, d);
+      if (wl >= d) x = combine<PROD>(y, x);
+    }
+    if (wl == 31) s_tot[w][0] = x;  // G == 256 rows; rows 0..7 reused for warp totals
+    __syncthreads();
+    double wexcl = ident, all = ident;
+    for (int k = 0; k < 8; ++k) {
+      const double t = s_tot[k][0];
+      if (k < w) wexcl = combine<PROD>(wexcl, t);
+      all = combine<PROD>(all, t);
+    }
+    const double incl_in_warp = x;
+    double prev = __shfl_up_sync(0xffffffffu, incl_in_warp, 1);
+    if (wl == 0) prev = ident;
+    excl = combine<PROD>(wexcl, prev);
+    tile_total = all;
+  } else {
+    s_tot[grp][lane] = run;
+    __syncthreads();
+    double all = ident;
+    for (int g = 0; g < G; ++g) {
+      const double t = s_tot[g][lane];
+      if (g < grp) excl = combine<PROD>(excl, t);
+      all = combine<PROD>(all, t);
+    }
+    tile_total = all;
+  }
+
+  // 3. publish and look back (warp 0, one data lane per thread lane)
+  if (threadIdx.x < 32) {
+    const int dl = threadIdx.x;
+    const uint32_t ep = a.epoch << 2;
+    // Thread dl < LT of warp 0 carries data lane dl (threads 0..LT-1 form
+    // step group 0); for LT == 1 the tile total is uniform across threads.
+    const double my_total = tile_total;
+    const bool publish = (tile != a.fault_tile);
+    double prefix = ident;
+    if (q == 0) {
+      if (publish) {
+        if (dl < LT) a.incl[tile * LT + dl] = my_total;
+        __threadfence();
+        __syncwarp();
+        if (dl == 0) atomicExch(&a.flags[tile], ep | kFlagIncl);
+      }
+    } else {
+      if (publish) {
+        if (dl < LT) a.agg[tile * LT + dl] = my_total;
+        __threadfence();
+        __syncwarp();
+        if (dl == 0) atomicExch(&a.flags[tile], ep | kFlagAgg);
+      }
+      int64_t j = tile - 1;
+      while (true) {
+        // lane 0 waits (bounded) and broadcasts, so control stays warp-uniform
+        uint32_t f = 0u;
+        int gave_up = 0;
+        if (dl == 0) {
+          f = load_flag(&a.flags[j]);
+          if ((f & ~3u) != ep || (f & 3u) == 0u) {
+            const uint64_t t0 = global_timer_ns();
+            uint32_t spins = 0;
+            while (true) {
+              f = load_flag(&a.flags[j]);
+              if ((f & ~3u) == ep && (f & 3u) != 0u) break;
+              if (load_flag(&a.control->scan_abort) == a.epoch) { gave_up = 1; break; }
+              if ((int64_t)(global_timer_ns() - t0) > a.timeout_ns || ++spins > (1u << 26)) {
+                gave_up = 1;
+                raise_status(a.control, 1, (int32_t)(tile & 0x7fffffff));
+                atomicExch(&a.control->scan_abort, a.epoch);
+                break;
+              }
+              __nanosleep(64);
+            }
+          }
+        }
+        f = __shfl_sync(0xffffffffu, f, 0);
+        gave_up = __shfl_sync(0xffffffffu, gave_up, 0);
+        if (gave_up) break;
+        __threadfence();
+        const bool inc = (f & 3u) == kFlagIncl;
+        const double pv = (dl < LT) ? __ldcg(inc ? &a.incl[j * LT + dl] : &a.agg[j * LT + dl]) : ident;
+        prefix = combine<PROD>(pv, prefix);
+        if (inc) break;
+        --j;
+      }
+      // publish the inclusive prefix (also after giving up, so that later
+      // tiles never wait on this one)
+      if (publish) {
+        if (dl < LT) a.incl[tile * LT + dl] = combine<PROD>(prefix, my_total);
+        __threadfence();
+        __syncwarp();
+        if (dl == 0) atomicExch(&a.flags[tile], ep | kFlagIncl);
+      }
+    }
+    if (dl < LT) s_prefix[dl] = prefix;
+  }
+  __syncthreads();
+
+  // 4. write outputs
+  const double base = combine<PROD>(s_prefix[lane], excl);
+#pragma unroll
+  for (int k = 0; k < SEG; ++k) {
+    const int64_t r = r0 + k;
+    if (lane_ok && r < a.R) out[r * a.orr] = (T)combine<PROD>(base, v[k]);
+  }
+
+  // 5. the last CTA to finish resets the ticket counters
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    const unsigned int d = atomicAdd(&a.control->counters[2], 1u);
+    if (d == (unsigned int)(a.ntiles - 1)) {
+      atomicExch(&a.control->counters[1], 0u);
+      atomicExch(&a.control->counters[2], 0u);
+    }
+  }
+}
+
+// Collapses the view around `axis` into (L, R, O); returns false when the
+// dims before or after the axis cannot be merged for both in and out.
+static bool split_axis(const acd_desc *in, const acd_desc *out, int axis, int64_t &L, int64_t &R, int64_t &O,
+                       int64_t *s_in, int64_t *s_out) {
+  auto merge = [&](int d0, int d1, int64_t &n, int64_t &si, int64_t &so) -> bool {
+    n = 1;
+    si = 0;
+    so = 0;
+    bool first = true;
+    int64_t ei = 0, eo = 0;
+    for (int d = d0; d < d1; ++d) {
+      if (in->shape[d] == 1) continue;
+      if (first) {
+        si = in->stride[d];
+        so = out->stride[d];
+        ei = si * in->shape[d];
+        eo = so * in->shape[d];
+        n = in->shape[d];
+        first = false;
+      } else {
+        if (in->stride[d] != ei || out->stride[d] != eo) return false;
+        n *= in->shape[d];
+        ei = in->stride[d] * in->shape[d];
+        eo = out->stride[d] * in->shape[d];
+      }
+    }
+    return true;
+  };
+  if (!merge(0, axis, L, s_in[0], s_out[0])) return false;
+  if (!merge(axis + 1, in->ndim, O, s_in[2], s_out[2])) return false;
+  R = in->shape[axis];
+  s_in[1] = in->stride[axis];
+  s_out[1] = out->stride[axis];
+  return true;
+}
+
+template <typename T, bool PROD>
+static acd_status launch_scan(acd_ctx *ctx, ScanArgs a, cudaStream_t s) {
+  constexpr int LTW = 128 / sizeof(T);  // lanes per tile when L > 1: 128-byte rows
+  const int LT = a.L == 1 ? 1 : LTW;
+  constexpr int SEG1 = 16, SEGW = 32;
+  const int RT = LT == 1 ? 256 * SEG1 : (256 / LTW) * SEGW;
+  a.lblocks = (a.L + LT - 1) / LT;
+  a.rtiles = (a.R + RT - 1) / RT;
+  a.ntiles = a.lblocks * a.O * a.rtiles;
+  if (a.ntiles > 0x7fffffffLL) return fail(ACD_ERR_UNSUPPORTED, "scan: too many tiles");
+  const size_t fbytes = (size_t)a.ntiles * sizeof(uint32_t);
+  const size_t foff = 0;
+  const size_t aoff = (fbytes + 255) / 256 * 256;
+  const size_t dbytes = (size_t)a.ntiles * LT * sizeof(double);
+  const size_t ioff = aoff + (dbytes + 255) / 256 * 256;
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, ioff + dbytes, s, &scratch));
+  char *base = static_cast<char *>(scratch);
+  a.flags = reinterpret_cast<uint32_t *>(base + foff);
+  a.agg = reinterpret_cast<double *>(base + aoff);
+  a.incl = reinterpret_cast<double *>(base + ioff);
+  a.control = ctx->control;
+  ctx->epoch = (ctx->epoch + 1) & 0x3fffffffu;
+  if (ctx->epoch == 0) ctx->epoch = 1;
+  a.epoch = ctx->epoch;
+  a.fault_tile = ctx->scan_fault_tile;
+  a.timeout_ns = ctx->scan_timeout_ns;
+  if (LT == 1)
+    k_scan<T, PROD, 1, SEG1><<<(int)a.ntiles, 256, 0, s>>>(a);
+  else
+    k_scan<T, PROD, LTW, SEGW><<<(int)a.ntiles, 256, 0, s>>>(a);
+  return ACD_OK;
+}
+
+}  // namespace acd
+
+using namespace acd;
+
+extern "C" {
+
+acd_status acd_scan(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis,
+                    acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_scan: null context");
+  ACD_TRY(check_desc(out, "out"));
+  ACD_TRY(check_desc(in, "in"));
+  if (op != ACD_CUMSUM && op != ACD_CUMPROD) return fail(ACD_ERR_INVALID, "acd_scan: bad op %d", op);
+  if (!is_float(in->dtype) || out->dtype != in->dtype)
+    return fail(ACD_ERR_DTYPE, "acd_scan: float32/float64 input and output of one dtype required");
+  if (out->ndim != in->ndim) return fail(ACD_ERR_SHAPE, "acd_scan: output rank differs");
+  for (int d = 0; d < in->ndim; ++d)
+    if (out->shape[d] != in->shape[d]) return fail(ACD_ERR_SHAPE, "acd_scan: output extent differs on axis %d", d);
+  if (axis >= in->ndim && in->ndim > 0) return fail(ACD_ERR_AXIS, "acd_scan: axis %d out of range", axis);
+  const int64_t n = desc_numel(in);
+  if (n == 0) return ACD_OK;
+  ScanArgs a{};
+  a.in = desc_ptr(in);
+  a.out = desc_ptr(out);
+  int64_t si[3] = {0, 0, 0}, so[3] = {0, 0, 0};
+  if (axis < 0 || in->ndim == 0) {
+    // flattened column-major order: both views must be contiguous
+    if (!desc_is_contiguous(in) || !desc_is_contiguous(out))
+      return fail(ACD_ERR_UNSUPPORTED, "acd_scan: flattened scan needs contiguous input and output");
+    a.L = 1;
+    a.R = n;
+    a.O = 1;
+    si[1] = so[1] = 1;
+  } else {
+    if (!split_axis(in, out, axis, a.L, a.R, a.O, si, so))
+      return fail(ACD_ERR_UNSUPPORTED, "acd_scan: view not collapsible around the axis; make it contiguous first");
+  }
+  a.sl = si[0];
+  a.sr = si[1];
+  a.so = si[2];
+  a.ol = so[0];
+  a.orr = so[1];
+  a.oo = so[2];
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  const bool prod = op == ACD_CUMPROD;
+  if (in->dtype == ACD_FLOAT32)
+    st = prod ? launch_scan<float, true>(ctx, a, s) : launch_scan<float, false>(ctx, a, s);
+  else
+    st = prod ? launch_scan<double, true>(ctx, a, s) : launch_scan<double, false>(ctx, a, s);
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,219 @@
+/*
+ * acd.h — C ABI of the B200 tensor hot path (elementwise, broadcast, strided
+ * copy, full/axis reductions, arg-reductions, scans, softmax).
+ *
+ * Every entry point is `extern "C"`, takes plain pointers and sizes, is
+ * stream-ordered (asynchronous with respect to the host unless stated) and
+ * returns an acd_status.  No exception crosses this boundary.  The message of
+ * the last failure on the calling thread is available from acd_last_error().
+ *
+ * Layout convention: acediaR tensors are column-major (src/gpuTensor.h:51-55,
+ * compute_strides at src/gpuTensor.h:359-370): axis 0 is the fastest-varying,
+ * stride[0] == 1 for a contiguous tensor.  A descriptor may describe any
+ * strided view: permuted, transposed, broadcast (stride 0) or offset.  The
+ * offset is applied exactly once (the reference applies it twice, src/gpuTensor.h:597-599
+ * with src/cuda_utils.h:140-146).
+ *
+ * Replaces, in the reference:
+ *   - cuda_utils::TensorDescriptor (src/cuda_utils.h:111-156): int32 shape and
+ *     strides, row-major linear_to_coords        -> acd_desc (int64, column-major)
+ *   - the TensorRegistry dtype dispatch (src/TensorRegistry.h:214-1386)
+ *                                                 -> dtype field + internal dispatch
+ *   - the extern "C" launchers (src/kernels/tensor_ops.cu:484-2037,
+ *     src/kernels/tensor_kernels.cu:934-1482)     -> the acd_* functions below.
+ * The reference's own launcher names are also exported by the same library;
+ * see acediar_launchers.h.
+ */
+#ifndef ACD_H
+#define ACD_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define ACD_MAX_DIMS 8
+
+/* Element types.  Names follow dtype_to_string (src/gpuTensor.h:183-200). */
+typedef enum {
+  ACD_FLOAT32 = 0, /* "float"  */
+  ACD_FLOAT64 = 1, /* "double" */
+  ACD_INT32 = 2,   /* "int32"  */
+  ACD_INT64 = 3,   /* "int64"  */
+  ACD_BOOL = 4     /* "bool", one byte holding 0 or 1 */
+} acd_dtype;
+
+typedef enum {
+  ACD_OK = 0,
+  ACD_ERR_INVALID = 1,     /* null pointer, bad ndim, negative extent, bad op code */
+  ACD_ERR_SHAPE = 2,       /* shapes not broadcastable, or output shape mismatch */
+  ACD_ERR_DTYPE = 3,       /* dtype combination not supported by the op */
+  ACD_ERR_AXIS = 4,        /* axis out of range */
+  ACD_ERR_ALLOC = 5,       /* workspace allocation failed */
+  ACD_ERR_CUDA = 6,        /* CUDA runtime error (message has the CUDA error string) */
+  ACD_ERR_DEVICE = 7,      /* a kernel raised its device status word (bounded wait expired) */
+  ACD_ERR_UNSUPPORTED = 8  /* valid request outside what this build implements */
+} acd_status;
+
+/* Strided view descriptor.  Element (c0..c_{n-1}) lives at
+ * data + (offset + sum_k c_k * stride[k]) * sizeof(dtype).  ndim == 0 is a
+ * one-element scalar.  Strides are in elements and may be 0 (broadcast). */
+typedef struct acd_desc {
+  void *data;
+  int64_t offset;
+  int64_t shape[ACD_MAX_DIMS];
+  int64_t stride[ACD_MAX_DIMS];
+  int32_t ndim;
+  int32_t dtype;
+} acd_desc;
+
+/* Opaque per-device context: owns the reduction/scan workspace and the
+ * device status word.  Calls that share one context must be ordered on one
+ * stream (the workspace is reused without locking). */
+typedef struct acd_ctx acd_ctx;
+
+/* cudaStream_t, passed as an opaque pointer so this header needs no CUDA headers. */
+typedef void *acd_stream;
+
+/* Optional allocator used for the workspace (e.g. a caller's caching pool).
+ * alloc returns NULL on failure. */
+typedef void *(*acd_alloc_fn)(size_t bytes, void *user);
+typedef void (*acd_free_fn)(void *ptr, void *user);
+
+/* ---- elementwise op codes ---------------------------------------------- */
+typedef enum {
+  ACD_EXP = 0, ACD_LOG = 1, ACD_SQRT = 2, ACD_ABS = 3, ACD_FLOOR = 4,
+  ACD_CEIL = 5, ACD_ROUND = 6, ACD_ERF = 7, ACD_TANH = 8, ACD_SIGMOID = 9,
+  ACD_RELU = 10, ACD_SIN = 11, ACD_COS = 12, ACD_NEG = 13, ACD_SQUARE = 14,
+  ACD_COPY = 15
+} acd_unary_op;
+
+typedef enum {
+  ACD_ADD = 0, ACD_SUB = 1, ACD_MUL = 2, ACD_DIV = 3,
+  ACD_MAX = 4, ACD_MIN = 5, ACD_POW = 6,
+  ACD_GT = 7, ACD_LT = 8, ACD_EQ = 9, ACD_NE = 10, ACD_GE = 11, ACD_LE = 12,
+  ACD_RSUB = 13, ACD_RDIV = 14 /* scalar-only: s - x, s / x */
+} acd_binary_op;
+
+/* Fused elementwise chains.  Each evaluates the listed R expression with one
+ * rounding per R operator, in the tensor dtype, so the result is bit-identical
+ * to issuing the operators one by one. */
+typedef enum {
+  ACD_FUSED_SCALE_ADD_EXP_NEG_SQUARE = 0, /* x*p0 + exp(-(x^2))          (one input)  */
+  ACD_FUSED_ADD_RELU = 1,                 /* relu(a + b)                 (two inputs) */
+  ACD_FUSED_TANH_SCALE = 2                /* tanh(x) * p0                (one input)  */
+} acd_fused_op;
+
+/* ---- reduction op codes ------------------------------------------------ */
+typedef enum {
+  ACD_RED_SUM = 0, ACD_RED_MEAN = 1, ACD_RED_MAX = 2, ACD_RED_MIN = 3,
+  ACD_RED_PROD = 4, ACD_RED_VAR = 5, /* sample variance, divisor n-1 */
+  ACD_RED_COUNT = 6                  /* number of non-zero elements */
+} acd_reduce_op;
+
+typedef enum { ACD_ARGMAX = 0, ACD_ARGMIN = 1 } acd_arg_op;
+typedef enum { ACD_CUMSUM = 0, ACD_CUMPROD = 1 } acd_scan_op;
+
+/* ---- context ----------------------------------------------------------- */
+const char *acd_version(void);
+const char *acd_last_error(void);
+const char *acd_status_string(acd_status s);
+
+/* Creates a context on `device` (the current device is left unchanged). */
+acd_status acd_ctx_create(int device, acd_ctx **out);
+acd_status acd_ctx_destroy(acd_ctx *ctx);
+/* Replaces the workspace allocator (NULL, NULL restores cudaMalloc/cudaFree).
+ * Frees the current workspace; safe only when no call on `ctx` is in flight. */
+acd_status acd_ctx_set_allocator(acd_ctx *ctx, acd_alloc_fn alloc, acd_free_fn free_fn, void *user);
+/* Reads and clears the device status word (synchronises `stream`).
+ * Returns ACD_ERR_DEVICE and fills *code when a kernel reported an error. */
+acd_status acd_ctx_check(acd_ctx *ctx, acd_stream stream, int32_t *code);
+/* Test hook for the bounded look-back wait of the scan: when `tile` >= 0,
+ * the scan kernel's tile with that index never publishes its prefix, so the
+ * tile after it gives up after `timeout_ns` and raises the status word.
+ * tile < 0 disables the hook.  timeout_ns <= 0 restores the default (1 s). */
+acd_status acd_ctx_set_scan_fault(acd_ctx *ctx, int64_t tile, int64_t timeout_ns);
+
+/* ---- shape helpers (host only, no CUDA) -------------------------------- */
+/* acediaR broadcast rule (src/gpuTensor.h:248-340): dims are aligned from the
+ * leading side; the shorter shape is tried at every offset, first fit wins. */
+acd_status acd_broadcast_shape(int32_t a_ndim, const int64_t *a_shape, int32_t b_ndim,
+                               const int64_t *b_shape, int32_t *out_ndim, int64_t *out_shape);
+/* Strides of `in` expanded to `out_ndim`/`out_shape` under the same rule
+ * (stride 0 on broadcast dims), cf. compute_broadcast_strides
+ * (src/TensorArithmetic.cpp:240-292). */
+acd_status acd_broadcast_strides(int32_t in_ndim, const int64_t *in_shape, const int64_t *in_stride,
+                                 int32_t out_ndim, const int64_t *out_shape, int64_t *out_stride);
+
+/* ---- elementwise ------------------------------------------------------- */
+/* out = op(in).  out and in have the same shape; in may be any strided view. */
+acd_status acd_unary(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, acd_stream stream);
+/* out = a op b with acediaR broadcasting.  Comparisons (GT..LE) write 0/1 as
+ * bool or in the input dtype, whichever `out` declares. */
+acd_status acd_binary(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *a,
+                      const acd_desc *b, acd_stream stream);
+/* out = in op s (s cast to the tensor dtype first, as elementwise_scalar_kernel
+ * does, src/kernels/tensor_kernels.cu:33-39).  ACD_POW with s == 2 is x*x. */
+acd_status acd_scalar(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, double s,
+                      acd_stream stream);
+/* Fused chains (acd_fused_op).  `b` is NULL for one-input chains. */
+acd_status acd_fused(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *a,
+                     const acd_desc *b, double p0, acd_stream stream);
+/* out = in, any strides on both sides (contiguous(), strided copy). */
+acd_status acd_copy(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream);
+
+/* ---- reductions -------------------------------------------------------- */
+/* Reduces the axes whose bit is set in axes_mask (bit k = axis k, 0-based).
+ * out holds prod(shape[k] for unreduced k) elements, in column-major order of
+ * the unreduced axes (keep.dims only changes the shape the caller reports).
+ * Output dtype: the input dtype, or FLOAT64 for FLOAT32/FLOAT64 input
+ * (wider result); COUNT writes INT32 or INT64; SUM of INT32 writes INT32
+ * (NA = INT32_MIN on overflow, as R) or INT64. */
+acd_status acd_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in,
+                      uint32_t axes_mask, acd_stream stream);
+/* Fused single pass over all elements: out_sum and out_var are one-element
+ * descriptors (either may be NULL).  Sum and sample variance as acd_reduce. */
+acd_status acd_sum_var(acd_ctx *ctx, const acd_desc *out_sum, const acd_desc *out_var,
+                       const acd_desc *in, acd_stream stream);
+/* Index of the first maximum (minimum) along `axis`, or over all elements in
+ * column-major order when axis < 0.  out dtype INT32 or INT64.  Indices are
+ * 1-based when one_based != 0 (which.max), else 0-based (the reference's
+ * axis kernel, src/kernels/tensor_kernels.cu:720-807).  NaN never wins. */
+acd_status acd_arg_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out_index,
+                          const acd_desc *out_value, const acd_desc *in, int32_t axis,
+                          int32_t one_based, acd_stream stream);
+
+/* ---- scans and softmax ------------------------------------------------- */
+/* Cumulative sum/product along `axis`, or over the column-major flattened
+ * tensor when axis < 0 (cumsum.gpuTensor, R/gpuTensor.R:2234-2277).
+ * Accumulates in float64 (float64 input: compensated float64). */
+acd_status acd_scan(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis,
+                    acd_stream stream);
+/* exp(x - max) / sum(exp(x - max)) along `axis`; axis < 0 normalises the
+ * whole tensor (tensor_softmax_*, src/kernels/tensor_ops.cu:826-846). */
+acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, int32_t axis,
+                       acd_stream stream);
+
+/* ---- sharded partials (multi-GPU global sum/var and argmax) ------------- */
+/* Writes this shard's partial statistics of all elements of `in` to the
+ * device array `stats` (float64[4]: n, shift, sum(x-shift), sum((x-shift)^2)),
+ * with shift = first element of the shard. */
+acd_status acd_stats_partial(acd_ctx *ctx, double *stats, const acd_desc *in, acd_stream stream);
+/* Argmax along `axis` written as order-preserving 64-bit keys (int64 array
+ * with one key per output): key = (ordered value bits << 32) | (0xFFFFFFFF - idx),
+ * sign bit flipped, so a signed MAX all-reduce selects the largest value and,
+ * among equal values, the smallest global index.  idx = local index +
+ * index_base.  FLOAT32 input only. */
+acd_status acd_argmax_keys(acd_ctx *ctx, int64_t *keys, const acd_desc *in, int32_t axis,
+                           int64_t index_base, acd_stream stream);
+/* Decodes keys back to indices (INT32/INT64 out, 1-based when one_based). */
+acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const int64_t *keys,
+                                  int32_t one_based, acd_stream stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* ACD_H */

@@ -1,0 +1,384 @@
+/*
+ * oracle.c — CPU restatement of the acediaR hot path in base-R semantics.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker of the CUDA path: only
+ * tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg load it.
+ * Nothing in the product (acedia-r_b200/) calls it.
+ *
+ * What it follows:
+ *   - elementwise formulas of the reference functors
+ *     (src/kernels/tensor_kernels.cuh:10-192): sigmoid = 1/(1+exp(-x)),
+ *     relu = fmax(x, 0), round = rint, max/min = fmax/fmin, comparisons 1/0;
+ *     each R operator rounds once in the tensor dtype (float ops are computed
+ *     in long double and rounded once, which is correctly rounded except in
+ *     rare double-rounding cases);
+ *   - reductions as base R computes them: sum in a long double accumulator,
+ *     mean as sum/n followed by R's correction pass mean += sum(x-mean)/n,
+ *     var two-pass with divisor n-1 (the reference also divides by n-1,
+ *     src/kernels/tensor_ops.cu:802), max/min NaN-ignoring like fmax;
+ *   - which.max / argmax: first index of the maximum (strict comparison,
+ *     src/kernels/tensor_kernels.cu:794; src/kernels/tensor_ops.cu:861-863);
+ *   - cumsum/cumprod: long double running accumulator, one rounding per
+ *     output (R/gpuTensor.R:2234-2277 runs base R's cumsum);
+ *   - softmax: exp(x - max) / sum(exp(x - max)) (src/kernels/tensor_ops.cu:826-846
+ *     for the whole tensor; per axis for the row softmax);
+ *   - strided copy: dest[idx] = src[sum coord*stride] in column-major order
+ *     (src/kernels/tensor_kernels.cu:272-295);
+ *   - axis reductions: output in column-major order of the kept axes
+ *     (src/kernels/tensor_kernels.cu:488-560, src/TensorRegistry.h:1153-1179).
+ * Layout: column-major (src/gpuTensor.h:359-370).  Every function takes int64
+ * shapes and element strides; outputs are contiguous column-major.
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define MAXD 8
+
+enum { DT_F32 = 0, DT_F64 = 1, DT_I32 = 2, DT_I64 = 3, DT_BOOL = 4 };
+enum {
+  U_EXP = 0, U_LOG, U_SQRT, U_ABS, U_FLOOR, U_CEIL, U_ROUND, U_ERF, U_TANH, U_SIGMOID, U_RELU, U_SIN, U_COS,
+  U_NEG, U_SQUARE, U_COPY
+};
+enum {
+  B_ADD = 0, B_SUB, B_MUL, B_DIV, B_MAX, B_MIN, B_POW, B_GT, B_LT, B_EQ, B_NE, B_GE, B_LE, B_RSUB, B_RDIV
+};
+enum { R_SUM = 0, R_MEAN, R_MAX, R_MIN, R_PROD, R_VAR, R_COUNT };
+
+static long double ld_get(const void *p, int dt, int64_t i) {
+  switch (dt) {
+    case DT_F32: return ((const float *)p)[i];
+    case DT_F64: return ((const double *)p)[i];
+    case DT_I32: return ((const int32_t *)p)[i];
+    case DT_I64: return (long double)((const int64_t *)p)[i];
+    case DT_BOOL: return ((const uint8_t *)p)[i];
+  }
+  return 0.0L;
+}
+
+/* round to the tensor dtype */
+static long double rnd(long double v, int dt) {
+  switch (dt) {
+    case DT_F32: return (float)v;
+    case DT_F64: return (double)v;
+    default: return v;
+  }
+}
+
+static void put(void *p, int dt, int64_t i, long double v) {
+  switch (dt) {
+    case DT_F32: ((float *)p)[i] = (float)v; break;
+    case DT_F64: ((double *)p)[i] = (double)v; break;
+    case DT_I32: ((int32_t *)p)[i] = (int32_t)v; break;
+    case DT_I64: ((int64_t *)p)[i] = (int64_t)v; break;
+    case DT_BOOL: ((uint8_t *)p)[i] = (uint8_t)(v != 0.0L); break;
+  }
+}
+
+static int64_t numel(int nd, const int64_t *shape) {
+  int64_t n = 1;
+  for (int d = 0; d < nd; ++d) n *= shape[d];
+  return n;
+}
+
+/* offset of the column-major linear index `idx` under `st` */
+static int64_t offset_of(int64_t idx, int nd, const int64_t *shape, const int64_t *st) {
+  int64_t off = 0;
+  for (int d = 0; d < nd; ++d) {
+    off += (idx % shape[d]) * st[d];
+    idx /= shape[d];
+  }
+  return off;
+}
+
+static long double unary(int op, long double x, int dt) {
+  switch (op) {
+    case U_EXP: return rnd(expl(x), dt);
+    case U_LOG: return rnd(logl(x), dt);
+    case U_SQRT: return rnd(sqrtl(x), dt);
+    case U_ABS: return fabsl(x);
+    case U_FLOOR: return floorl(x);
+    case U_CEIL: return ceill(x);
+    case U_ROUND: return rintl(x); /* half to even, as rint */
+    case U_ERF: return rnd(erfl(x), dt);
+    case U_TANH: return rnd(tanhl(x), dt);
+    case U_SIGMOID: {
+      const long double e = rnd(expl(-x), dt);
+      const long double d = rnd(1.0L + e, dt);
+      return rnd(1.0L / d, dt);
+    }
+    case U_RELU: return isnan(x) ? 0.0L : (x > 0.0L ? x : 0.0L); /* fmax(x, 0) */
+    case U_SIN: return rnd(sinl(x), dt);
+    case U_COS: return rnd(cosl(x), dt);
+    case U_NEG: return -x;
+    case U_SQUARE: return rnd(x * x, dt);
+    default: return x;
+  }
+}
+
+static long double fmaxl_r(long double a, long double b) {
+  if (isnan(a)) return b;
+  if (isnan(b)) return a;
+  return a > b ? a : b;
+}
+static long double fminl_r(long double a, long double b) {
+  if (isnan(a)) return b;
+  if (isnan(b)) return a;
+  return a < b ? a : b;
+}
+
+static long double binary(int op, long double a, long double b, int dt) {
+  switch (op) {
+    case B_ADD: return rnd(a + b, dt);
+    case B_SUB: return rnd(a - b, dt);
+    case B_MUL: return rnd(a * b, dt);
+    case B_DIV: return rnd(a / b, dt);
+    case B_MAX: return fmaxl_r(a, b);
+    case B_MIN: return fminl_r(a, b);
+    case B_POW: return (b == 2.0L) ? rnd(a * a, dt) : rnd(powl(a, b), dt);
+    case B_GT: return a > b;
+    case B_LT: return a < b;
+    case B_EQ: return a == b;
+    case B_NE: return a != b;
+    case B_GE: return a >= b;
+    case B_LE: return a <= b;
+    case B_RSUB: return rnd(b - a, dt);
+    case B_RDIV: return rnd(b / a, dt);
+  }
+  return 0.0L;
+}
+
+/* ---- elementwise ------------------------------------------------------- */
+void orc_unary(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, void *out) {
+  const int64_t n = numel(nd, shape);
+  for (int64_t i = 0; i < n; ++i) put(out, dt, i, unary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), dt));
+}
+
+/* a and b carry strides already expanded to `shape` (stride 0 on broadcast
+ * dims); out_dt is the input dtype or bool for comparisons */
+void orc_binary(int op, int dt, const void *a, const int64_t *sa, const void *b, const int64_t *sb, int nd,
+                const int64_t *shape, int out_dt, void *out) {
+  const int64_t n = numel(nd, shape);
+  for (int64_t i = 0; i < n; ++i) {
+    const long double x = ld_get(a, dt, offset_of(i, nd, shape, sa));
+    const long double y = ld_get(b, dt, offset_of(i, nd, shape, sb));
+    put(out, out_dt, i, binary(op, x, y, dt));
+  }
+}
+
+/* x op s, with s first cast to the tensor dtype */
+void orc_scalar(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, double s,
+                int out_dt, void *out) {
+  const int64_t n = numel(nd, shape);
+  const long double sv = rnd((long double)s, dt);
+  for (int64_t i = 0; i < n; ++i)
+    put(out, out_dt, i, binary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), sv, dt));
+}
+
+/* x*p + exp(-(x^2)), five roundings */
+void orc_gauss_chain(int dt, const void *in, int64_t n, double p, void *out) {
+  const long double pv = rnd(p, dt);
+  for (int64_t i = 0; i < n; ++i) {
+    const long double x = ld_get(in, dt, i);
+    const long double a = rnd(x * pv, dt);
+    const long double sq = rnd(x * x, dt);
+    const long double e = rnd(expl(-sq), dt);
+    put(out, dt, i, rnd(a + e, dt));
+  }
+}
+
+void orc_copy(int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, void *out) {
+  orc_unary(U_COPY, dt, in, nd, shape, st, out);
+}
+
+/* ---- reductions over a set of reduced values ---------------------------- */
+static long double r_mean(const long double *v, int64_t n) {
+  long double s = 0.0L;
+  for (int64_t i = 0; i < n; ++i) s += v[i];
+  s /= n;
+  if (isfinite(s)) {
+    long double t = 0.0L;
+    for (int64_t i = 0; i < n; ++i) t += v[i] - s;
+    s += t / n;
+  }
+  return s;
+}
+
+static long double reduce_vals(int op, const long double *v, int64_t n) {
+  switch (op) {
+    case R_SUM: {
+      long double s = 0.0L;
+      for (int64_t i = 0; i < n; ++i) s += v[i];
+      return s;
+    }
+    case R_MEAN: return r_mean(v, n);
+    case R_MAX: {
+      long double m = -INFINITY;
+      for (int64_t i = 0; i < n; ++i) m = fmaxl_r(m, v[i]);
+      return m;
+    }
+    case R_MIN: {
+      long double m = INFINITY;
+      for (int64_t i = 0; i < n; ++i) m = fminl_r(m, v[i]);
+      return m;
+    }
+    case R_PROD: {
+      long double p = 1.0L;
+      for (int64_t i = 0; i < n; ++i) p *= v[i];
+      return p;
+    }
+    case R_VAR: {
+      if (n < 2) return NAN;
+      const long double m = r_mean(v, n);
+      long double s = 0.0L;
+      for (int64_t i = 0; i < n; ++i) s += (v[i] - m) * (v[i] - m);
+      return s / (n - 1);
+    }
+    case R_COUNT: {
+      int64_t c = 0;
+      for (int64_t i = 0; i < n; ++i) c += v[i] != 0.0L;
+      return (long double)c;
+    }
+  }
+  return 0.0L;
+}
+
+/* Splits dims into kept/reduced; output index runs column-major over kept dims. */
+static void split(int nd, const int64_t *shape, const int64_t *st, uint32_t mask, int *nk, int64_t *ks, int64_t *kst,
+                  int *nr, int64_t *rs, int64_t *rst) {
+  *nk = *nr = 0;
+  for (int d = 0; d < nd; ++d) {
+    if ((mask >> d) & 1u) {
+      rs[*nr] = shape[d];
+      rst[*nr] = st[d];
+      (*nr)++;
+    } else {
+      ks[*nk] = shape[d];
+      kst[*nk] = st[d];
+      (*nk)++;
+    }
+  }
+}
+
+/* out (double) holds one value per kept element */
+int orc_reduce(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, uint32_t mask,
+               double *out) {
+  int nk, nr;
+  int64_t ks[MAXD], kst[MAXD], rs[MAXD], rst[MAXD];
+  split(nd, shape, st, mask, &nk, ks, kst, &nr, rs, rst);
+  const int64_t O = numel(nk, ks), R = numel(nr, rs);
+  long double *v = (long double *)malloc(sizeof(long double) * (R > 0 ? R : 1));
+  if (!v) return -1;
+  for (int64_t o = 0; o < O; ++o) {
+    const int64_t base = offset_of(o, nk, ks, kst);
+    for (int64_t j = 0; j < R; ++j) v[j] = ld_get(in, dt, base + offset_of(j, nr, rs, rst));
+    out[o] = (double)reduce_vals(op, v, R);
+  }
+  free(v);
+  return 0;
+}
+
+/* first index of the max (min); NaN never wins; -1 when none */
+int orc_arg_reduce(int is_max, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
+                   int one_based, int64_t *out) {
+  const uint32_t mask = axis < 0 ? 0xFFu : (1u << axis);
+  int nk, nr;
+  int64_t ks[MAXD], kst[MAXD], rs[MAXD], rst[MAXD];
+  split(nd, shape, st, mask, &nk, ks, kst, &nr, rs, rst);
+  const int64_t O = numel(nk, ks), R = numel(nr, rs);
+  for (int64_t o = 0; o < O; ++o) {
+    const int64_t base = offset_of(o, nk, ks, kst);
+    int64_t best = -1;
+    long double bv = 0.0L;
+    for (int64_t j = 0; j < R; ++j) {
+      const long double x = ld_get(in, dt, base + offset_of(j, nr, rs, rst));
+      if (isnan(x)) continue;
+      if (best < 0 || (is_max ? x > bv : x < bv)) {
+        best = j;
+        bv = x;
+      }
+    }
+    out[o] = best < 0 ? -1 : best + (one_based ? 1 : 0);
+  }
+  return 0;
+}
+
+/* cumsum/cumprod along `axis` (axis < 0: flattened column-major) */
+int orc_scan(int is_prod, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
+             void *out) {
+  const int64_t n = numel(nd, shape);
+  if (axis < 0) {
+    long double acc = is_prod ? 1.0L : 0.0L;
+    for (int64_t i = 0; i < n; ++i) {
+      const long double x = ld_get(in, dt, offset_of(i, nd, shape, st));
+      acc = is_prod ? acc * x : acc + x;
+      put(out, dt, i, acc);
+    }
+    return 0;
+  }
+  /* out is contiguous: stride of `axis` in out = prod(shape[<axis]) */
+  int64_t ostride = 1;
+  for (int d = 0; d < axis; ++d) ostride *= shape[d];
+  const int64_t R = shape[axis];
+  for (int64_t i = 0; i < n; ++i) {
+    const int64_t r = (i / ostride) % R;
+    if (r != 0) continue; /* start of a fiber */
+    long double acc = is_prod ? 1.0L : 0.0L;
+    for (int64_t k = 0; k < R; ++k) {
+      const int64_t oi = i + k * ostride;
+      const long double x = ld_get(in, dt, offset_of(oi, nd, shape, st));
+      acc = is_prod ? acc * x : acc + x;
+      put(out, dt, oi, acc);
+    }
+  }
+  return 0;
+}
+
+/* softmax along `axis` (axis < 0: whole tensor); exp in long double of the
+ * dtype-rounded difference, sum in long double */
+int orc_softmax(int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis, void *out) {
+  const int64_t n = numel(nd, shape);
+  if (n == 0) return 0;
+  int64_t ostride = 1, R = n;
+  if (axis >= 0) {
+    for (int d = 0; d < axis; ++d) ostride *= shape[d];
+    R = shape[axis];
+  }
+  long double *e = (long double *)malloc(sizeof(long double) * R);
+  if (!e) return -1;
+  for (int64_t i = 0; i < n; ++i) {
+    if (axis >= 0 && (i / ostride) % R != 0) continue;
+    if (axis < 0 && i != 0) break;
+    const int64_t step = axis >= 0 ? ostride : 1;
+    long double m = -INFINITY;
+    for (int64_t k = 0; k < R; ++k) m = fmaxl_r(m, ld_get(in, dt, offset_of(i + k * step, nd, shape, st)));
+    long double s = 0.0L;
+    for (int64_t k = 0; k < R; ++k) {
+      const long double d = rnd(ld_get(in, dt, offset_of(i + k * step, nd, shape, st)) - m, dt);
+      e[k] = expl(d);
+      s += e[k];
+    }
+    for (int64_t k = 0; k < R; ++k) put(out, dt, i + k * step, e[k] / s);
+  }
+  free(e);
+  return 0;
+}
+
+/* Fused sum and var of a contiguous array (for large-size checks and the CPU
+ * baseline): long double sum, two-pass variance. */
+void orc_sum_var(int dt, const void *in, int64_t n, double *sum, double *var) {
+  long double s = 0.0L;
+  for (int64_t i = 0; i < n; ++i) s += ld_get(in, dt, i);
+  long double m = s / n;
+  long double t = 0.0L;
+  for (int64_t i = 0; i < n; ++i) t += ld_get(in, dt, i) - m;
+  m += t / n;
+  long double q = 0.0L;
+  for (int64_t i = 0; i < n; ++i) {
+    const long double d = ld_get(in, dt, i) - m;
+    q += d * d;
+  }
+  *sum = (double)s;
+  *var = n > 1 ? (double)(q / (n - 1)) : NAN;
+}

@@ -1,0 +1,252 @@
+"""ctypes wrapper of the CPU oracle (oracle.c) — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg import
+this module; the product never does.
+
+Tensors are given as (buffer, shape, strides, offset) views over a 1-D numpy
+buffer in column-major element strides, or as numpy arrays, which are taken
+as logical R arrays (their column-major order is the storage order).  Results
+are numpy arrays of the logical shape.
+
+The broadcast rule is restated here from the reference (src/gpuTensor.h:248-340,
+src/TensorArithmetic.cpp:240-292): the shorter shape is tried at every offset
+from the leading side and the first fit wins.
+"""
+import ctypes
+import os
+import subprocess
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+_LIB = None
+_LIB_MT = None
+
+DT = {np.dtype(np.float32): 0, np.dtype(np.float64): 1, np.dtype(np.int32): 2, np.dtype(np.int64): 3,
+      np.dtype(np.uint8): 4, np.dtype(np.bool_): 4}
+UNARY = {n: i for i, n in enumerate(
+    ["exp", "log", "sqrt", "abs", "floor", "ceil", "round", "erf", "tanh", "sigmoid", "relu", "sin", "cos",
+     "neg", "square", "copy"])}
+BINARY = {n: i for i, n in enumerate(
+    ["add", "sub", "mul", "div", "max", "min", "pow", "gt", "lt", "eq", "ne", "ge", "le", "rsub", "rdiv"])}
+REDUCE = {n: i for i, n in enumerate(["sum", "mean", "max", "min", "prod", "var", "count"])}
+COMPARE = {"gt", "lt", "eq", "ne", "ge", "le"}
+
+_i64p = ctypes.POINTER(ctypes.c_int64)
+
+
+def build():
+    """Compiles liboracle*.so with the Makefile next to this file."""
+    subprocess.run(["make", "-s", "-C", HERE], check=True)
+
+
+def lib():
+    global _LIB
+    if _LIB is None:
+        path = os.path.join(HERE, "liboracle.so")
+        if not os.path.exists(path):
+            build()
+        _LIB = ctypes.CDLL(path)
+    return _LIB
+
+
+def lib_mt():
+    global _LIB_MT
+    if _LIB_MT is None:
+        path = os.path.join(HERE, "liboracle_mt.so")
+        if not os.path.exists(path):
+            build()
+        _LIB_MT = ctypes.CDLL(path)
+    return _LIB_MT
+
+
+class View:
+    """A strided view over a 1-D numpy buffer (column-major element strides)."""
+
+    def __init__(self, buf, shape, strides=None, offset=0):
+        self.buf = np.ascontiguousarray(buf).reshape(-1)
+        self.shape = tuple(int(s) for s in shape)
+        if strides is None:
+            strides, acc = [], 1
+            for s in self.shape:
+                strides.append(acc)
+                acc *= s
+        self.strides = tuple(int(s) for s in strides)
+        self.offset = int(offset)
+
+    @staticmethod
+    def of(x):
+        if isinstance(x, View):
+            return x
+        a = np.asarray(x)
+        return View(a.reshape(-1, order="F") if a.ndim else a.reshape(1), a.shape if a.ndim else (1,))
+
+    @property
+    def dtype(self):
+        return self.buf.dtype
+
+    def ptr(self):
+        return ctypes.c_void_p(self.buf.ctypes.data + self.offset * self.buf.itemsize)
+
+
+def _arr(v):
+    return (ctypes.c_int64 * max(1, len(v)))(*v)
+
+
+def _shape_out(shape):
+    return shape if len(shape) else (1,)
+
+
+def _result(flat, shape):
+    return flat.reshape(_shape_out(shape), order="F")
+
+
+def broadcast_shape(a, b):
+    """acediaR broadcast shape (leading-side offset sweep); raises ValueError."""
+    a, b = tuple(a), tuple(b)
+    if len(a) == len(b):
+        offs = [(a, b, 0)]
+    else:
+        short, long_ = (a, b) if len(a) < len(b) else (b, a)
+        offs = [(short, long_, o) for o in range(len(long_) - len(short) + 1)]
+    for short, long_, off in offs:
+        ok = True
+        for i in range(len(long_)):
+            ds = short[i - off] if off <= i < off + len(short) else 1
+            if ds != long_[i] and ds != 1 and long_[i] != 1:
+                ok = False
+                break
+        if ok:
+            return tuple(max(short[i - off] if off <= i < off + len(short) else 1, long_[i])
+                         for i in range(len(long_)))
+    raise ValueError("Tensor shapes are not broadcastable")
+
+
+def broadcast_strides(shape, strides, out_shape):
+    for off in range(len(out_shape) - len(shape) + 1):
+        if all(s == d or s == 1 or d == 1 for s, d in zip(shape, out_shape[off:off + len(shape)])):
+            st = [0] * len(out_shape)
+            for i, (s, sd) in enumerate(zip(shape, strides)):
+                st[off + i] = 0 if s == 1 else sd
+            return tuple(st)
+    raise ValueError("Shape mismatch in broadcast stride calculation")
+
+
+# ---------------------------------------------------------------------------
+def unary(op, x):
+    v = View.of(x)
+    out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
+    lib().orc_unary(UNARY[op], DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
+                    out.ctypes.data_as(ctypes.c_void_p))
+    return _result(out, v.shape)
+
+
+def copy(x):
+    return unary("copy", x)
+
+
+def binary(op, a, b, out_dtype=None):
+    va, vb = View.of(a), View.of(b)
+    shape = broadcast_shape(va.shape, vb.shape)
+    sa = broadcast_strides(va.shape, va.strides, shape)
+    sb = broadcast_strides(vb.shape, vb.strides, shape)
+    odt = np.dtype(out_dtype) if out_dtype is not None else (np.dtype(np.uint8) if op in COMPARE else va.dtype)
+    out = np.empty(int(np.prod(shape)), dtype=odt)
+    lib().orc_binary(BINARY[op], DT[va.dtype], va.ptr(), _arr(sa), vb.ptr(), _arr(sb), len(shape), _arr(shape),
+                     DT[odt], out.ctypes.data_as(ctypes.c_void_p))
+    return _result(out, shape)
+
+
+def scalar(op, x, s, out_dtype=None):
+    v = View.of(x)
+    odt = np.dtype(out_dtype) if out_dtype is not None else (np.dtype(np.uint8) if op in COMPARE else v.dtype)
+    out = np.empty(int(np.prod(v.shape)), dtype=odt)
+    lib().orc_scalar(BINARY[op], DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
+                     ctypes.c_double(s), DT[odt], out.ctypes.data_as(ctypes.c_void_p))
+    return _result(out, v.shape)
+
+
+def gauss_chain(x, p=0.5):
+    """x*p + exp(-(x^2)) with one rounding per R operator."""
+    a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))
+    out = np.empty_like(a)
+    lib().orc_gauss_chain(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                          ctypes.c_double(p), out.ctypes.data_as(ctypes.c_void_p))
+    return out.reshape(np.asarray(x).shape, order="F")
+
+
+def reduce(op, x, axes=None):
+    """Base-R reduction over `axes` (0-based list; None = all).  Returns float64."""
+    v = View.of(x)
+    nd = len(v.shape)
+    axes = list(range(nd)) if axes is None else list(axes)
+    mask = 0
+    for a in axes:
+        mask |= 1 << a
+    kept = [v.shape[d] for d in range(nd) if d not in axes]
+    out = np.empty(max(1, int(np.prod(kept))), dtype=np.float64)
+    lib().orc_reduce(REDUCE[op], DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides),
+                     ctypes.c_uint32(mask), out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+    return out.reshape(kept, order="F") if kept else out[0]
+
+
+def arg_reduce(op, x, axis=None, one_based=True):
+    v = View.of(x)
+    nd = len(v.shape)
+    kept = [v.shape[d] for d in range(nd) if axis is not None and d != axis]
+    out = np.empty(max(1, int(np.prod(kept))), dtype=np.int64)
+    lib().orc_arg_reduce(1 if op == "argmax" else 0, DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides),
+                         -1 if axis is None else int(axis), 1 if one_based else 0,
+                         out.ctypes.data_as(_i64p))
+    return out.reshape(kept, order="F") if axis is not None else int(out[0])
+
+
+def scan(op, x, axis=None):
+    v = View.of(x)
+    out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
+    lib().orc_scan(1 if op == "cumprod" else 0, DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape),
+                   _arr(v.strides), -1 if axis is None else int(axis), out.ctypes.data_as(ctypes.c_void_p))
+    return _result(out, v.shape)
+
+
+def softmax(x, axis=None):
+    v = View.of(x)
+    out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
+    lib().orc_softmax(DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
+                      -1 if axis is None else int(axis), out.ctypes.data_as(ctypes.c_void_p))
+    return _result(out, v.shape)
+
+
+def sum_var(x):
+    a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))
+    s, q = ctypes.c_double(), ctypes.c_double()
+    lib().orc_sum_var(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size), ctypes.byref(s),
+                      ctypes.byref(q))
+    return s.value, q.value
+
+
+def pipeline_views(x, threads=1):
+    """The strided-views step on CPU: returns (y, z, sum, var, argmax_axis1)."""
+    x = np.asarray(x, dtype=np.float32)
+    n0, n1, n2 = x.shape
+    xf = np.ascontiguousarray(x.reshape(-1, order="F"))
+    y = np.empty(xf.size, dtype=np.float32)
+    z = np.empty(xf.size, dtype=np.float32)
+    idx = np.empty(n0 * n1, dtype=np.int32)
+    s, v = ctypes.c_double(), ctypes.c_double()
+    lib_mt().orc_pipeline_views(xf.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(n0), ctypes.c_int64(n1),
+                                ctypes.c_int64(n2), y.ctypes.data_as(ctypes.c_void_p),
+                                z.ctypes.data_as(ctypes.c_void_p), ctypes.byref(s), ctypes.byref(v),
+                                idx.ctypes.data_as(ctypes.c_void_p), ctypes.c_int(threads))
+    return (y.reshape((n2, n0, n1), order="F"), z.reshape((n2, n0, n1), order="F"), s.value, v.value,
+            idx.reshape((n0, n1), order="F"))
+
+
+def pipeline_views_raw(xf, n0, n1, n2, y, z, idx, threads):
+    """Same as pipeline_views on preallocated flat buffers (for timing)."""
+    s, v = ctypes.c_double(), ctypes.c_double()
+    lib_mt().orc_pipeline_views(xf.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(n0), ctypes.c_int64(n1),
+                                ctypes.c_int64(n2), y.ctypes.data_as(ctypes.c_void_p),
+                                z.ctypes.data_as(ctypes.c_void_p), ctypes.byref(s), ctypes.byref(v),
+                                idx.ctypes.data_as(ctypes.c_void_p), ctypes.c_int(threads))
+    return s.value, v.value

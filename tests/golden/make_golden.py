@@ -1,0 +1,218 @@
+"""Generates tests/golden/reference_cases.json.
+
+The cases are the known-answer tests of the reference's testthat suite
+(tests/testthat/*.R of acediaR), transcribed as inputs plus the base-R
+expression each test compares against.  The expected values are computed
+here with numpy on the logical (column-major) arrays, following the R
+expression named in each case — independently of the C oracle and of the
+CUDA library, which are both checked against this file.
+
+Run:  python tests/golden/make_golden.py
+"""
+import json
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+
+
+def col(a):
+    """Flat column-major list of a logical array."""
+    return np.asarray(a).reshape(-1, order="F").tolist()
+
+
+def rmatrix(data, nrow, ncol):
+    return np.asarray(data, dtype=np.float64).reshape((nrow, ncol), order="F")
+
+
+def rarray(data, dims):
+    return np.asarray(data, dtype=np.float64).reshape(dims, order="F")
+
+
+def t_in(a, dtype="float"):
+    a = np.asarray(a, dtype=np.float64)
+    return {"data": col(a), "shape": list(a.shape) if a.ndim else [1], "dtype": dtype}
+
+
+def r_sweep(x, margin, stats, fn):
+    """R's sweep(x, MARGIN, STATS, FUN) for the margins used by the tests."""
+    x = np.asarray(x)
+    stats = np.asarray(stats)
+    shape = [1] * x.ndim
+    for i, m in enumerate(margin):
+        shape[m - 1] = x.shape[m - 1]
+    s = stats.reshape([x.shape[m - 1] for m in margin], order="F")
+    # place the stats on the margin axes, singleton elsewhere
+    full = np.empty(x.shape)
+    it = np.nditer(x, flags=["multi_index"])
+    for _ in it:
+        idx = it.multi_index
+        full[idx] = s[tuple(idx[m - 1] for m in margin)]
+    return fn(x, full)
+
+
+cases = []
+
+
+def case(cid, source, op, inputs, expected, **args):
+    e = np.asarray(expected)
+    cases.append({
+        "id": cid, "source": source, "op": op, "inputs": inputs, "args": args,
+        "expected": {"data": col(e) if e.ndim else [e.item()], "shape": list(e.shape) if e.ndim else [1]},
+    })
+
+
+def case_error(cid, source, op, inputs, pattern, **args):
+    cases.append({"id": cid, "source": source, "op": op, "inputs": inputs, "args": args, "error": pattern})
+
+
+AX = "tests/testthat/test-axis-aware-reductions.R"
+m12 = rmatrix(np.arange(1, 13), 3, 4)
+a24 = rarray(np.arange(1, 25), (2, 3, 4))
+mext = rmatrix([3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8], 3, 4)
+mprod = rmatrix([1, 2, 1, 2, 1, 2, 1, 2, 1, 2, 1, 2], 3, 4)
+
+case("sum_axis1", AX + ":21-36", "sum", [t_in(m12)], m12.sum(axis=0), axis=[1])           # colSums
+case("sum_axis2", AX + ":38-42", "sum", [t_in(m12)], m12.sum(axis=1), axis=[2])           # rowSums
+case("sum_axis1_keep", AX + ":44-47", "sum", [t_in(m12)], m12.sum(axis=0, keepdims=True), axis=[1], keep_dims=True)
+case("sum_axis2_keep", AX + ":49-51", "sum", [t_in(m12)], m12.sum(axis=1, keepdims=True), axis=[2], keep_dims=True)
+case("sum_axes12", AX + ":54-62", "sum", [t_in(a24)], a24.sum(axis=(0, 1)), axis=[1, 2])  # apply(x, 3, sum)
+case("sum_axes12_keep", AX + ":64-67", "sum", [t_in(a24)], a24.sum(axis=(0, 1), keepdims=True), axis=[1, 2],
+     keep_dims=True)
+case("sum_global", AX + ":70-78", "sum", [t_in(m12)], m12.sum())
+case("mean_axis1", AX + ":84-93", "mean", [t_in(m12)], m12.mean(axis=0), axis=[1])       # colMeans
+case("mean_axis2", AX + ":95-99", "mean", [t_in(m12)], m12.mean(axis=1), axis=[2])       # rowMeans
+case("max_axis1", AX + ":107-116", "max", [t_in(mext)], mext.max(axis=0), axis=[1])
+case("max_axis2", AX + ":118-122", "max", [t_in(mext)], mext.max(axis=1), axis=[2])
+case("min_axis1", AX + ":125-133", "min", [t_in(mext)], mext.min(axis=0), axis=[1])
+case("min_axis2", AX + ":135-139", "min", [t_in(mext)], mext.min(axis=1), axis=[2])
+case("prod_axis1", AX + ":145-155", "prod", [t_in(mprod)], mprod.prod(axis=0), axis=[1])
+case("prod_axis2", AX + ":157-161", "prod", [t_in(mprod)], mprod.prod(axis=1), axis=[2])
+v = col(mext)
+case("argmax_global", AX + ":167-176", "which.max", [t_in(mext)], int(np.argmax(v)) + 1)
+case("argmin_global", AX + ":167-176", "which.min", [t_in(mext)], int(np.argmin(v)) + 1)
+case("sum_transposed_axis1", AX + ":215-224", "sum", [t_in(m12)], m12.T.sum(axis=0), axis=[1], transpose=True)
+case("sum_transposed_axis2", AX + ":226-228", "sum", [t_in(m12)], m12.T.sum(axis=1), axis=[2], transpose=True)
+case("sum_double", AX + ":244-248", "sum", [t_in(m12, "double")], m12.sum(axis=0), axis=[1])
+case("sum_1d_axis", AX + ":254-261", "sum", [t_in([1, 2, 3, 4, 5])], np.float64(15), axis=[1])
+case("sum_single_axis", AX + ":263-266", "sum", [t_in([42])], np.float64(42), axis=[1])
+case("var_axis1", AX + ":273-279", "var", [t_in(m12)], m12.var(axis=0, ddof=1), axis=[1])
+case("var_axis2", AX + ":281-282", "var", [t_in(m12)], m12.var(axis=1, ddof=1), axis=[2])
+for a in (5, 0, -1, 1.5):
+    case_error("axis_invalid_%s" % str(a).replace(".", "_").replace("-", "m"), AX + ":192-207", "sum",
+               [t_in(m12)], "axis must be a vector of positive integers", axis=[a])
+
+EX = "tests/testthat/test-range-extrema-helpers.R"
+for cid, data, dt, line in [("wmax_1d", [3, 1, 4, 1, 5, 9, 2, 6], "float", "118-128"),
+                            ("wmax_f32", [1.5, 4.9, 2.7, 0.3, 1.1], "float", "130-145"),
+                            ("wmax_f64", [1.5, 4.9, 2.7, 0.3, 1.1], "double", "130-145"),
+                            ("wmax_single", [42], "float", "158-162"),
+                            ("wmax_ties", [5, 2, 5, 1, 5, 3], "float", "164-169"),
+                            ("wmax_negative", [-5, -1, -10, -3, -7], "float", "171-175"),
+                            ("wmax_all_same", [3.14] * 5, "float", "177-181")]:
+    case(cid, EX + ":" + line, "which.max", [t_in(data, dt)], int(np.argmax(data)) + 1)
+case("wmax_matrix", EX + ":147-155", "which.max", [t_in(mext)], int(np.argmax(col(mext))) + 1)
+m33 = rmatrix([1, 8, 3, 2, 9, 4, 5, 1, 6], 3, 3)
+case("wmax_transposed", EX + ":185-195", "which.max", [t_in(m33)], int(np.argmax(col(m33.T))) + 1, transpose=True)
+for cid, data, dt, line in [("wmin_1d", [3, 1, 4, 1, 5, 9, 2, 6], "float", "203-212"),
+                            ("wmin_f32", [1.5, 0.3, 2.7, 4.9, 1.1], "float", "214-229"),
+                            ("wmin_f64", [1.5, 0.3, 2.7, 4.9, 1.1], "double", "214-229"),
+                            ("wmin_ties", [5, 2, 5, 2, 3, 2], "float", "248-254")]:
+    case(cid, EX + ":" + line, "which.min", [t_in(data, dt)], int(np.argmin(data)) + 1)
+case("wmin_matrix", EX + ":231-240", "which.min", [t_in(mext)], int(np.argmin(col(mext))) + 1)
+
+CU = "tests/testthat/test-cumulative-operations.R"
+case("cumsum_1d", CU + ":25-37", "cumsum", [t_in([1, 2, 3, 4, 5])], np.cumsum([1, 2, 3, 4, 5.0]))
+case("cumsum_f32", CU + ":39-48", "cumsum", [t_in([1.5, 2.7, 3.1, 4.9])], np.cumsum([1.5, 2.7, 3.1, 4.9]))
+case("cumsum_f64", CU + ":50-55", "cumsum", [t_in([1.5, 2.7, 3.1, 4.9], "double")],
+     np.cumsum([1.5, 2.7, 3.1, 4.9]))
+case("cumsum_matrix", CU + ":58-69", "cumsum", [t_in(m12)],
+     np.cumsum(col(m12)).reshape((3, 4), order="F"))
+case("cumsum_single", CU + ":71-75", "cumsum", [t_in([42])], np.array([42.0]))
+case("cumsum_negative", CU + ":88-96", "cumsum", [t_in([-1, 2, -3, 4, -5])], np.cumsum([-1, 2, -3, 4, -5.0]))
+case("cumprod_1d", CU + ":99-111", "cumprod", [t_in([1, 2, 1.5, 1.2, 1.1])], np.cumprod([1, 2, 1.5, 1.2, 1.1]))
+case("cumprod_f32", CU + ":113-122", "cumprod", [t_in([1.1, 1.2, 1.05, 0.9])], np.cumprod([1.1, 1.2, 1.05, 0.9]))
+case("cumprod_f64", CU + ":124-129", "cumprod", [t_in([1.1, 1.2, 1.05, 0.9], "double")],
+     np.cumprod([1.1, 1.2, 1.05, 0.9]))
+mcp = rmatrix([1, 1.1, 1.2, 0.9, 1.05, 1.15], 2, 3)
+case("cumprod_matrix", CU + ":132-143", "cumprod", [t_in(mcp)], np.cumprod(col(mcp)).reshape((2, 3), order="F"))
+case("cumprod_single", CU + ":145-150", "cumprod", [t_in([3.14])], np.array([3.14]))
+
+CO = "tests/testthat/test-comparison-operators.R"
+a5, b5 = np.array([1, 2, 3, 2, 1.0]), np.array([1, 3, 3, 2, 2.0])
+for op, f in [("==", np.equal), ("!=", np.not_equal), ("<", np.less), ("<=", np.less_equal), (">", np.greater),
+              (">=", np.greater_equal)]:
+    case("cmp_%s" % {"==": "eq", "!=": "ne", "<": "lt", "<=": "le", ">": "gt", ">=": "ge"}[op], CO + ":25-250", op,
+         [t_in(a5), t_in(b5)], f(a5, b5).astype(np.float64))
+    case("cmp_scalar_%s" % {"==": "eq", "!=": "ne", "<": "lt", "<=": "le", ">": "gt", ">=": "ge"}[op],
+         CO + ":40-250", op, [t_in(a5)], f(a5, 2.0).astype(np.float64), scalar=2.0)
+d27 = np.array([1.5, 2.7, 3.1, 2.7])
+case("cmp_eq_f32_2_7", CO + ":51-59", "==", [t_in(d27)], (np.float32(d27) == np.float32(2.7)).astype(float),
+     scalar=2.7)
+case("cmp_eq_f64_2_7", CO + ":61-65", "==", [t_in(d27, "double")], (d27 == 2.7).astype(float), scalar=2.7)
+m6 = rmatrix([1, 2, 3, 4, 5, 6], 2, 3)
+v3 = np.array([2, 3, 4.0])
+case("cmp_bcast_gt", CO + ":273-285", ">", [t_in(m6), t_in(v3)], r_sweep(m6, [2], v3, np.greater).astype(float))
+case("cmp_bcast_eq", CO + ":287-292", "==", [t_in(m6), t_in(v3)], r_sweep(m6, [2], v3, np.equal).astype(float))
+
+BR = "tests/testthat/test-comprehensive-broadcasting.R"
+v10 = np.array([10, 20, 30.0])
+case("bcast_mat_vec", BR + ":25-37", "+", [t_in(m6), t_in(v10)], r_sweep(m6, [2], v10, np.add))
+case("bcast_vec_mat", BR + ":39-41", "+", [t_in(v10), t_in(m6)], r_sweep(m6, [2], v10, np.add))
+case("bcast_3d_mat", BR + ":43-55", "+", [t_in(a24), t_in(m6)], r_sweep(a24, [1, 2], m6, np.add))
+m6b = rmatrix([10, 20, 30, 40, 50, 60], 2, 3)
+case("bcast_sub", BR + ":57-76", "-", [t_in(m6b), t_in([1, 2, 3])], r_sweep(m6b, [2], np.array([1, 2, 3.0]),
+                                                                           np.subtract))
+ta = rarray([1, 2, 3, 4, 5, 6], (2, 1, 3))
+tb = rarray([10, 20, 30, 40], (1, 4, 1))
+case("bcast_multi", BR + ":264-286", "+", [t_in(ta), t_in(tb)], ta + tb)
+sa = rarray([1, 2, 3, 4, 5, 6], (3, 1, 2))
+sb = rarray([2, 3, 4, 5], (1, 4, 1))
+case("bcast_singleton_mul", BR + ":288-306", "*", [t_in(sa), t_in(sb)], sa * sb)
+r13 = rmatrix([1, 2, 3], 1, 3)
+m23 = rmatrix([10, 20, 30, 40, 50, 60], 2, 3)
+case("bcast_row", BR + ":308-320", "+", [t_in(r13), t_in(m23)], r13 + m23)
+c31 = rmatrix([1, 2, 3], 3, 1)
+m34 = rmatrix(np.arange(10, 130, 10), 3, 4)
+case("bcast_col", BR + ":322-335", "+", [t_in(c31), t_in(m34)], c31 + m34)
+case("bcast_transposed", BR + ":370-387", "+", [t_in(m6), t_in([10, 20])],
+     r_sweep(m6.T, [2], np.array([10, 20.0]), np.add), transpose_first=True)
+case_error("bcast_error_2d", BR + ":392-405", "+", [t_in(rmatrix(np.arange(1, 7), 2, 3)),
+                                                     t_in(rmatrix(np.arange(1, 9), 2, 4))], "shape|dimension|broadcast")
+case_error("bcast_error_3d", BR + ":406-411", "+", [t_in(rarray(np.arange(1, 13), (2, 2, 3))),
+                                                     t_in(rmatrix(np.arange(1, 9), 4, 2))], "shape|dimension|broadcast")
+
+CC = "tests/testthat/test-consolidated-core.R"
+d5 = np.array([-2, -1, 0, 1, 2.0])
+case("act_tanh", CC + ":369-377", "tanh", [t_in(d5)], np.tanh(d5))
+case("act_sigmoid", CC + ":379-383", "sigmoid", [t_in(d5)], 1 / (1 + np.exp(-d5)))
+dr = np.array([-3, -1, 0, 1, 3.0])
+case("act_relu", CC + ":385-390", "relu", [t_in(dr)], np.maximum(dr, 0))
+e = np.exp(d5 - d5.max())
+case("softmax_1d", CC + ":392-404", "softmax", [t_in(d5)], e / e.sum())
+d15 = np.array([1, 2, 3, 4, 5.0])
+case("prod_global", CC + ":555-558", "prod", [t_in(d15)], np.float64(120))
+case("var_global", CC + ":560-563", "var", [t_in(d15)], np.float64(d15.var(ddof=1)))
+
+VM = "tests/testthat/test-consolidated-views-memory.R"
+case("permute_231", VM + ":80-93", "permute", [t_in(a24)], np.transpose(a24, (1, 2, 0)), perm=[2, 3, 1])
+case("permute_312", VM + ":98-101", "permute", [t_in(a24)], np.transpose(a24, (2, 0, 1)), perm=[3, 1, 2])
+case("permute_132", VM + ":103-104", "permute", [t_in(a24)], np.transpose(a24, (0, 2, 1)), perm=[1, 3, 2])
+case("permute_identity", VM + ":107-108", "permute", [t_in(a24)], a24, perm=[1, 2, 3])
+m34v = rmatrix(np.arange(1, 13), 3, 4)
+case("contiguous_transposed", VM + ":128-146", "permute", [t_in(m34v)], m34v.T, perm=[2, 1])
+
+
+def main():
+    out = {"generator": "tests/golden/make_golden.py",
+           "note": "inputs and base-R expressions transcribed from the reference testthat suite; expected values "
+                   "computed with numpy on column-major logical arrays",
+           "cases": cases}
+    with open(os.path.join(HERE, "reference_cases.json"), "w") as f:
+        json.dump(out, f, indent=1)
+    print("wrote %d cases" % len(cases))
+
+
+if __name__ == "__main__":
+    main()

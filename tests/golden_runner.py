@@ -1,0 +1,87 @@
+"""Runs one golden case (tests/golden/reference_cases.json) through either
+the CPU oracle or the CUDA path (the acediar mirror of the R API)."""
+import numpy as np
+
+import oracle
+
+_OPS = {"+": "add", "-": "sub", "*": "mul", "/": "div", "==": "eq", "!=": "ne", "<": "lt", "<=": "le", ">": "gt",
+        ">=": "ge"}
+_NP = {"float": np.float32, "double": np.float64}
+
+
+def _host(inp):
+    return np.asarray(inp["data"], dtype=_NP[inp["dtype"]]).reshape(inp["shape"], order="F")
+
+
+def _transposed_view(a):
+    """The transpose view of a 2-D column-major array (strides swapped)."""
+    v = oracle.View.of(a)
+    return oracle.View(v.buf, (v.shape[1], v.shape[0]), (v.strides[1], v.strides[0]))
+
+
+def run_oracle(case):
+    op, args = case["op"], case["args"]
+    xs = [_host(i) for i in case["inputs"]]
+    if op in ("sum", "mean", "max", "min", "prod", "var"):
+        x = _transposed_view(xs[0]) if args.get("transpose") else oracle.View.of(xs[0])
+        axis = args.get("axis")
+        for a in axis or []:
+            if not (isinstance(a, int) and 1 <= a <= len(x.shape)):
+                raise ValueError("axis must be a vector of positive integers")
+        r = oracle.reduce(op, x, None if axis is None else [a - 1 for a in axis])
+        return np.asarray(r)
+    if op in ("which.max", "which.min"):
+        x = _transposed_view(xs[0]) if args.get("transpose") else oracle.View.of(xs[0])
+        return oracle.arg_reduce("argmax" if op == "which.max" else "argmin", x, None, True)
+    if op in ("cumsum", "cumprod"):
+        return oracle.scan(op, xs[0])
+    if op in _OPS:
+        if "scalar" in args:
+            return oracle.scalar(_OPS[op], xs[0], args["scalar"])
+        a = _transposed_view(xs[0]) if args.get("transpose_first") else xs[0]
+        return oracle.binary(_OPS[op], a, xs[1])
+    if op in ("tanh", "sigmoid", "relu"):
+        return oracle.unary(op, xs[0])
+    if op == "softmax":
+        return oracle.softmax(xs[0])
+    if op == "permute":
+        v = oracle.View.of(xs[0])
+        perm = [p - 1 for p in args["perm"]]
+        return oracle.copy(oracle.View(v.buf, [v.shape[p] for p in perm], [v.strides[p] for p in perm]))
+    raise KeyError(op)
+
+
+def run_gpu(acd, case):
+    op, args = case["op"], case["args"]
+    dts = [i["dtype"] for i in case["inputs"]]
+    xs = [acd.as_tensor(_host(i), dtype=d) for i, d in zip(case["inputs"], dts)]
+    if op in ("sum", "mean", "max", "min", "prod", "var"):
+        x = acd.transpose_view(xs[0]) if args.get("transpose") else xs[0]
+        f = getattr(acd, op)
+        axis = args.get("axis")
+        r = f(x, axis=axis, keep_dims=args.get("keep_dims", False))
+        return np.asarray(r.as_array() if hasattr(r, "as_array") else r)
+    if op in ("which.max", "which.min"):
+        x = acd.transpose_view(xs[0]) if args.get("transpose") else xs[0]
+        return acd.which_max(x) if op == "which.max" else acd.which_min(x)
+    if op in ("cumsum", "cumprod"):
+        return getattr(acd, op)(xs[0]).as_array()
+    if op in _OPS:
+        a = acd.transpose_view(xs[0]) if args.get("transpose_first") else xs[0]
+        b = args["scalar"] if "scalar" in args else xs[1]
+        r = {"+": lambda: a + b, "-": lambda: a - b, "*": lambda: a * b, "/": lambda: a / b,
+             "==": lambda: a == b, "!=": lambda: a != b, "<": lambda: a < b, "<=": lambda: a <= b,
+             ">": lambda: a > b, ">=": lambda: a >= b}[op]()
+        return r.as_array()
+    if op in ("tanh", "sigmoid", "relu"):
+        return getattr(acd, op)(xs[0]).as_array()
+    if op == "softmax":
+        return acd.softmax(xs[0]).as_array()
+    if op == "permute":
+        return acd.contiguous(acd.permute_view(xs[0], args["perm"])).as_array()
+    raise KeyError(op)
+
+
+def expected_of(case):
+    e = case["expected"]
+    return np.asarray(e["data"], dtype=np.float64).reshape(e["shape"], order="F")

@@ -1,0 +1,99 @@
+"""cumsum/cumprod and softmax: CUDA path vs the oracle (relative 1e-5 for
+float32, 1e-12 for float64)."""
+import ctypes
+
+import numpy as np
+import pytest
+
+import oracle
+from helpers import assert_rel
+
+pytestmark = pytest.mark.gpu
+TOL = {"float": 1e-5, "double": 1e-12}
+NP = {"float": np.float32, "double": np.float64}
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_cumsum_flattened(acd, name):
+    rng = np.random.default_rng(1)
+    for n in [1, 2, 31, 4095, 4096, 4097, 100003, (1 << 22) + 9]:
+        x = rng.uniform(0, 1, n).astype(NP[name])
+        got = acd.cumsum(acd.as_tensor(x, dtype=name)).as_array()
+        assert_rel(got, oracle.scan("cumsum", x), TOL[name], "cumsum n=%d" % n)
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_cumprod_flattened(acd, name):
+    rng = np.random.default_rng(2)
+    for n in [1, 7, 5000, 70001]:
+        x = rng.uniform(0.999, 1.001, n).astype(NP[name])
+        got = acd.cumprod(acd.as_tensor(x, dtype=name)).as_array()
+        assert_rel(got, oracle.scan("cumprod", x), TOL[name] * 10, "cumprod n=%d" % n)
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_cumsum_along_axes(acd, name):
+    rng = np.random.default_rng(3)
+    for shape in [(64, 100000), (3, 5000), (33, 257), (1000, 6), (8, 300, 5), (1, 9000), (70, 2, 9)]:
+        x = rng.uniform(0, 1, shape).astype(NP[name])
+        t = acd.as_tensor(x, dtype=name)
+        for axis in range(1, len(shape) + 1):
+            got = acd.cumsum(t, axis=axis).as_array()
+            assert_rel(got, oracle.scan("cumsum", x, axis - 1), TOL[name], "cumsum %s axis %d" % (shape, axis))
+        got = acd.cumsum(t).as_array()
+        assert_rel(got, oracle.scan("cumsum", x), TOL[name], "cumsum %s flat" % (shape,))
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_cumsum_of_view(acd, name):
+    rng = np.random.default_rng(4)
+    x = rng.uniform(0, 1, (50, 70)).astype(NP[name])
+    v = acd.transpose_view(acd.as_tensor(x, dtype=name))
+    for axis in (1, 2):
+        got = acd.cumsum(v, axis=axis).as_array()
+        assert_rel(got, oracle.scan("cumsum", x.T, axis - 1), TOL[name], "cumsum transposed axis %d" % axis)
+
+
+def test_scan_bounded_wait_reports_and_recovers(acd):
+    """A tile that never publishes makes its successor's wait expire: the
+    kernel returns, the status word is raised, and the context stays usable."""
+    import acediar._lib as L
+    import acediar.tensor as T
+    x = np.ones(4096 * 8, dtype=np.float32)
+    t = acd.as_tensor(x, dtype="float")
+    lib = L.lib()
+    ctx = T.context()
+    acd.check_device_status()  # clean start
+    L.check(lib.acd_ctx_set_scan_fault(ctx, 3, 20_000_000))  # tile 3 never publishes; 20 ms limit
+    try:
+        acd.cumsum(t)
+        with pytest.raises(L.AcdError) as ei:
+            acd.check_device_status()
+        assert ei.value.status == 7
+    finally:
+        L.check(lib.acd_ctx_set_scan_fault(ctx, -1, 0))
+    got = acd.cumsum(t).as_array()  # the context still works
+    np.testing.assert_array_equal(got, np.arange(1, x.size + 1, dtype=np.float32))
+    acd.check_device_status()
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_softmax_along_axes(acd, name):
+    rng = np.random.default_rng(5)
+    for shape in [(65, 4096), (1000, 33), (7, 3000), (33, 64, 5), (4, 40000), (2048, 8)]:
+        x = (rng.normal(0, 2, shape) + rng.uniform(-50, 50, (shape[0],) + (1,) * (len(shape) - 1))).astype(NP[name])
+        t = acd.as_tensor(x, dtype=name)
+        for axis in range(1, len(shape) + 1):
+            got = acd.softmax(t, axis=axis).as_array()
+            exp = oracle.softmax(x, axis - 1)
+            assert_rel(got, exp, TOL[name], "softmax %s axis %d" % (shape, axis), atol=1e-300)
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
+def test_softmax_whole_tensor(acd, name):
+    rng = np.random.default_rng(6)
+    for n in [1, 5, 1000, (1 << 20) + 1]:
+        x = rng.normal(0, 3, n).astype(NP[name])
+        got = acd.softmax(acd.as_tensor(x, dtype=name)).as_array()
+        assert_rel(got, oracle.softmax(x), TOL[name], "softmax n=%d" % n, atol=1e-300)
+        assert abs(got.astype(np.float64).sum() - 1.0) < (1e-4 if name == "float" else 1e-10)
