@@ -67,7 +67,8 @@ def merge_stats_torch(rows):
 
 def pack_keys_np(values, index):
     """Host reference of the key format written by acd_argmax_keys."""
-    v = np.ascontiguousarray(values, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    # -0 and +0 share one key (the reduction treats them as equal)
+    v = (np.ascontiguousarray(values, dtype=np.float32) + np.float32(0.0)).view(np.uint32).astype(np.uint64)
     ordered = np.where(v & 0x80000000, (~v) & 0xFFFFFFFF, v | 0x80000000)
     u = (ordered << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(index, dtype=np.uint64))
     return (u ^ np.uint64(0x8000000000000000)).view(np.int64)

@@ -14,8 +14,8 @@ Reference semantics kept on purpose:
     softmax / per-axis scan;
   - which.max / argmax indices are 1-based with the first-index tie rule.
 """
+import builtins
 import ctypes
-import math
 import numbers
 
 import numpy as np
@@ -142,7 +142,7 @@ def _is_contig(shape, strides):
 def _alloc(shape, dtype, device=None):
     n = int(np.prod(shape)) if len(shape) else 1
     dev = device if device is not None else torch.device("cuda", torch.cuda.current_device())
-    storage = torch.empty(max(n, 1), dtype=_TORCH[dtype], device=dev)
+    storage = torch.empty(builtins.max(n, 1), dtype=_TORCH[dtype], device=dev)
     return gpuTensor(storage, shape, dtype)
 
 
@@ -238,14 +238,13 @@ def _arith(op, a, b, dtype_out=None):
         big, one = (a, b) if b.size == 1 else (b, a)
         one_b = gpuTensor(one.storage, big.shape, one.dtype, (0,) * len(big.shape), one.offset)
         a, b = (big, one_b) if b.size == 1 else (one_b, big)
+    if a.shape == b.shape:
+        shp = a.shape
     else:
         try:
             shp = L.broadcast_shape(a.shape, b.shape)
         except L.AcdError:
             raise ValueError("Tensor shapes are not broadcastable")
-        if shp != a.shape or shp != b.shape:
-            pass
-    shp = a.shape if a.shape == b.shape else L.broadcast_shape(a.shape, b.shape)
     odt = ("bool" if dtype_out is None else a.dtype) if cmp else a.dtype
     out = _alloc(shp, odt, a.device)
     L.check(L.lib().acd_binary(context(), L.BINARY[op], ctypes.byref(out.desc()), ctypes.byref(a.desc()),

@@ -69,8 +69,12 @@ struct acd_ctx {
   int sm_count = 148;
   int max_smem_optin = 0;
   acd::Control *control = nullptr;  // device, persistent, zeroed at creation
-  void *scratch = nullptr;          // device, grows on demand, zeroed when (re)allocated
+  void *scratch = nullptr;          // device, grows on demand: partial results (no state at rest)
   size_t scratch_bytes = 0;
+  unsigned int *counters = nullptr; // device, grows on demand, zero at rest (kernels reset them)
+  size_t counters_n = 0;
+  uint32_t *flags = nullptr;        // device, grows on demand, epoch-tagged scan tile flags
+  size_t flags_n = 0;
   uint32_t epoch = 0;               // incremented per scan launch (tags tile flags)
   acd_alloc_fn alloc = nullptr;
   acd_free_fn free_fn = nullptr;
@@ -81,9 +85,14 @@ struct acd_ctx {
 
 namespace acd {
 
-// Returns a zero-initialised-at-allocation scratch region of at least
-// `bytes`.  Growing synchronises `stream` first (the old region may be in use).
+// Scratch for partial results: at least `bytes`, contents undefined.
+// Growing synchronises `stream` first (the old region may be in use).
 acd_status get_scratch(acd_ctx *ctx, size_t bytes, cudaStream_t stream, void **out);
+// `n` tile counters, zero at rest: every kernel that increments one resets it.
+// Nothing else ever writes this region.
+acd_status get_counters(acd_ctx *ctx, size_t n, cudaStream_t stream, unsigned int **out);
+// `n` scan tile flags tagged with the launch epoch (stale tags never match).
+acd_status get_flags(acd_ctx *ctx, size_t n, cudaStream_t stream, uint32_t **out);
 // Device guard: makes ctx->device current for the scope.
 struct DeviceGuard {
   int prev = -1;

@@ -70,10 +70,42 @@ acd_status get_scratch(acd_ctx *ctx, size_t bytes, cudaStream_t stream, void **o
   }
   void *p = dev_alloc(ctx, want);
   if (!p) return fail(ACD_ERR_ALLOC, "workspace allocation of %zu bytes failed", want);
-  ACD_CUDA(cudaMemsetAsync(p, 0, want, stream));
   ctx->scratch = p;
   ctx->scratch_bytes = want;
   *out = p;
+  return ACD_OK;
+}
+
+template <typename W>
+static acd_status get_zeroed(acd_ctx *ctx, W **region, size_t *have, size_t n, cudaStream_t stream,
+                             const char *what) {
+  if (n == 0) n = 1;
+  if (*region && *have >= n) return ACD_OK;
+  size_t want = n < 2 * *have ? 2 * *have : n;
+  want = (want + 1023) & ~(size_t)1023;
+  if (*region) {
+    ACD_CUDA(cudaStreamSynchronize(stream));
+    dev_free(ctx, *region);
+    *region = nullptr;
+    *have = 0;
+  }
+  void *p = dev_alloc(ctx, want * sizeof(W));
+  if (!p) return fail(ACD_ERR_ALLOC, "%s allocation of %zu bytes failed", what, want * sizeof(W));
+  ACD_CUDA(cudaMemsetAsync(p, 0, want * sizeof(W), stream));
+  *region = static_cast<W *>(p);
+  *have = want;
+  return ACD_OK;
+}
+
+acd_status get_counters(acd_ctx *ctx, size_t n, cudaStream_t stream, unsigned int **out) {
+  ACD_TRY(get_zeroed(ctx, &ctx->counters, &ctx->counters_n, n, stream, "counter"));
+  *out = ctx->counters;
+  return ACD_OK;
+}
+
+acd_status get_flags(acd_ctx *ctx, size_t n, cudaStream_t stream, uint32_t **out) {
+  ACD_TRY(get_zeroed(ctx, &ctx->flags, &ctx->flags_n, n, stream, "flag"));
+  *out = ctx->flags;
   return ACD_OK;
 }
 
@@ -225,6 +257,8 @@ acd_status acd_ctx_destroy(acd_ctx *ctx) {
   DeviceGuard g(ctx->device);
   cudaDeviceSynchronize();
   dev_free(ctx, ctx->scratch);
+  dev_free(ctx, ctx->counters);
+  dev_free(ctx, ctx->flags);
   cudaFree(ctx->control);
   delete ctx;
   return ACD_OK;
@@ -235,12 +269,16 @@ acd_status acd_ctx_set_allocator(acd_ctx *ctx, acd_alloc_fn alloc, acd_free_fn f
   if ((alloc == nullptr) != (free_fn == nullptr))
     return fail(ACD_ERR_INVALID, "acd_ctx_set_allocator: alloc and free must both be set or both be NULL");
   DeviceGuard g(ctx->device);
-  if (ctx->scratch) {
-    ACD_CUDA(cudaDeviceSynchronize());
-    dev_free(ctx, ctx->scratch);
-    ctx->scratch = nullptr;
-    ctx->scratch_bytes = 0;
-  }
+  ACD_CUDA(cudaDeviceSynchronize());
+  dev_free(ctx, ctx->scratch);
+  dev_free(ctx, ctx->counters);
+  dev_free(ctx, ctx->flags);
+  ctx->scratch = nullptr;
+  ctx->scratch_bytes = 0;
+  ctx->counters = nullptr;
+  ctx->counters_n = 0;
+  ctx->flags = nullptr;
+  ctx->flags_n = 0;
   ctx->alloc = alloc;
   ctx->free_fn = free_fn;
   ctx->alloc_user = user;

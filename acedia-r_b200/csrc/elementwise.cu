@@ -188,31 +188,58 @@ __global__ void __launch_bounds__(kEwThreads) k_general(typename F::Out *__restr
 }
 
 // out(i,j,k) = in(i,j,k) where out is contiguous along i and in along j.
-// Persistent over 2-D tiles of TILE x TILE, batched over k.
+// Persistent over TILE x TILE tiles (batched over k).  Tiles are visited in
+// diagonal order: tile t of a batch has i-tile t % tiles0 and j-tile
+// (t / tiles0 + t % tiles0) % tiles1, a bijection under which the tiles that
+// run at the same time spread over both the input's and the output's
+// contiguous address ranges (a plain row order puts every concurrent tile at
+// the same low address bits when the other side's stride is a power of two,
+// which concentrates the traffic on a few memory channels).  Full tiles with
+// aligned rows use 16-byte loads and stores.
 template <typename T, int TILE>
 __global__ void __launch_bounds__(256) k_transpose(T *__restrict__ out, const T *__restrict__ in, int64_t n0,
                                                    int64_t n1, int64_t n2, int64_t os1, int64_t os2, int64_t is0,
-                                                   int64_t is2, int64_t tiles0, int64_t tiles1) {
+                                                   int64_t is2, int64_t tiles0, int64_t tiles1, int vec_ok) {
+  constexpr int V = (sizeof(T) >= 4) ? 16 / (int)sizeof(T) : 1;
   __shared__ T tile[TILE][TILE + 1];
-  const int64_t ntiles = tiles0 * tiles1 * n2;
+  const int64_t nt01 = tiles0 * tiles1;
+  const int64_t ntiles = nt01 * n2;
   for (int64_t t = blockIdx.x; t < ntiles; t += gridDim.x) {
-    const int64_t t01 = t % (tiles0 * tiles1);
-    const int64_t k = t / (tiles0 * tiles1);
-    const int64_t i0 = (t01 % tiles0) * TILE;
-    const int64_t j0 = (t01 / tiles0) * TILE;
+    const int64_t k = t / nt01;
+    const int64_t t01 = t - k * nt01;
+    const int64_t ti = t01 % tiles0;
+    const int64_t tj = (t01 / tiles0 + ti) % tiles1;
+    const int64_t i0 = ti * TILE, j0 = tj * TILE;
     const T *src = in + k * is2;
     T *dst = out + k * os2;
     const bool full = (i0 + TILE <= n0) && (j0 + TILE <= n1);
-    // read rows i (strided by is0), contiguous along j
-    for (int e = threadIdx.x; e < TILE * TILE; e += blockDim.x) {
-      const int r = e / TILE, c = e % TILE;
-      if (full || (i0 + r < n0 && j0 + c < n1)) tile[r][c] = src[(i0 + r) * is0 + j0 + c];
-    }
-    __syncthreads();
-    // write columns j (strided by os1), contiguous along i
-    for (int e = threadIdx.x; e < TILE * TILE; e += blockDim.x) {
-      const int r = e / TILE, c = e % TILE;
-      if (full || (i0 + c < n0 && j0 + r < n1)) dst[(i0 + c) + (j0 + r) * os1] = tile[c][r];
+    if (V > 1 && full && vec_ok) {
+      // rows i, contiguous along j: TILE/V vectors per row
+      for (int e = threadIdx.x; e < TILE * (TILE / V); e += blockDim.x) {
+        const int r = e / (TILE / V), cv = e % (TILE / V);
+        const Vec<T, V> x = *reinterpret_cast<const Vec<T, V> *>(src + (i0 + r) * is0 + j0 + cv * V);
+#pragma unroll
+        for (int q = 0; q < V; ++q) tile[r][cv * V + q] = x.v[q];
+      }
+      __syncthreads();
+      // columns j, contiguous along i
+      for (int e = threadIdx.x; e < TILE * (TILE / V); e += blockDim.x) {
+        const int r = e / (TILE / V), cv = e % (TILE / V);
+        Vec<T, V> y;
+#pragma unroll
+        for (int q = 0; q < V; ++q) y.v[q] = tile[cv * V + q][r];
+        *reinterpret_cast<Vec<T, V> *>(dst + (i0 + cv * V) + (j0 + r) * os1) = y;
+      }
+    } else {
+      for (int e = threadIdx.x; e < TILE * TILE; e += blockDim.x) {
+        const int r = e / TILE, c = e % TILE;
+        if (full || (i0 + r < n0 && j0 + c < n1)) tile[r][c] = src[(i0 + r) * is0 + j0 + c];
+      }
+      __syncthreads();
+      for (int e = threadIdx.x; e < TILE * TILE; e += blockDim.x) {
+        const int r = e / TILE, c = e % TILE;
+        if (full || (i0 + c < n0 && j0 + r < n1)) dst[(i0 + c) + (j0 + r) * os1] = tile[c][r];
+      }
     }
     __syncthreads();
   }
@@ -298,10 +325,13 @@ static acd_status launch_map(acd_ctx *ctx, const F &f, const acd_desc *out, cons
 template <typename T, int TILE>
 static void launch_transpose(acd_ctx *ctx, T *out, const T *in, int64_t n0, int64_t n1, int64_t n2, int64_t os1,
                              int64_t os2, int64_t is0, int64_t is2, cudaStream_t stream) {
+  constexpr int V = (sizeof(T) >= 4) ? 16 / (int)sizeof(T) : 1;
   const int64_t tiles0 = (n0 + TILE - 1) / TILE, tiles1 = (n1 + TILE - 1) / TILE;
   const int64_t ntiles = tiles0 * tiles1 * n2;
   const int grid = grid_for(ctx, ntiles, 1, 8);
-  k_transpose<T, TILE><<<grid, 256, 0, stream>>>(out, in, n0, n1, n2, os1, os2, is0, is2, tiles0, tiles1);
+  const int vec_ok = V > 1 && is0 % V == 0 && os1 % V == 0 && is2 % V == 0 && os2 % V == 0 &&
+                     aligned_to<T>(in, 16) && aligned_to<T>(out, 16);
+  k_transpose<T, TILE><<<grid, 256, 0, stream>>>(out, in, n0, n1, n2, os1, os2, is0, is2, tiles0, tiles1, vec_ok);
 }
 
 // Bitwise copy between two views of one element size.

@@ -4,7 +4,8 @@
 // called for exp/log/tanh/erf/sin/cos (their documented ulp bounds apply).
 //
 // Formulas follow the reference functors (src/kernels/tensor_kernels.cuh:10-192):
-// sigmoid = 1/(1+exp(-x)), relu = fmax(x, 0), round = rint (half to even),
+// sigmoid = 1/(1+exp(-x)) (float32: evaluated in double, one rounding),
+// relu = fmax(x, 0), round = rint (half to even),
 // max/min = fmax/fmin (NaN-ignoring), comparisons write 1 or 0.  Two
 // deliberate differences, both toward base R: x/s is a true division (the
 // reference multiplies by 1/s, src/kernels/tensor_ops.cu:1901-1913), and x^2
@@ -63,7 +64,14 @@ __device__ __forceinline__ T unary_apply(T x) {
   else if constexpr (OP == ACD_ROUND) return m_rint(x);
   else if constexpr (OP == ACD_ERF) return m_erf(x);
   else if constexpr (OP == ACD_TANH) return m_tanh(x);
-  else if constexpr (OP == ACD_SIGMOID) return T(1) / (T(1) + m_exp(-x));
+  else if constexpr (OP == ACD_SIGMOID) {
+    // sigmoid() is one R function: float32 is evaluated in double and rounded
+    // once (as base R would); float64 keeps the reference formula's roundings
+    if constexpr (std::is_same<T, float>::value)
+      return (float)(1.0 / (1.0 + exp(-(double)x)));
+    else
+      return T(1) / (T(1) + m_exp(-x));
+  }
   else if constexpr (OP == ACD_RELU) return m_max(x, T(0));
   else if constexpr (OP == ACD_SIN) return m_sin(x);
   else if constexpr (OP == ACD_COS) return m_cos(x);

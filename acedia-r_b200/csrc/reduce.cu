@@ -555,10 +555,10 @@ static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t
       chunk = (chunk + 4 * V - 1) / (4 * V) * (4 * V);
       S = (p.R + chunk - 1) / chunk;
       void *scratch;
-      const size_t cbytes = align_up(sizeof(unsigned int) * p.O, 256);
-      ACD_TRY(get_scratch(ctx, cbytes + sizeof(Acc) * p.O * S, stream, &scratch));
-      unsigned int *counters = static_cast<unsigned int *>(scratch);
-      Acc *partials = reinterpret_cast<Acc *>(static_cast<char *>(scratch) + cbytes);
+      unsigned int *counters;
+      ACD_TRY(get_counters(ctx, (size_t)p.O, stream, &counters));
+      ACD_TRY(get_scratch(ctx, sizeof(Acc) * p.O * S, stream, &scratch));
+      Acc *partials = static_cast<Acc *>(scratch);
       const int64_t grid = p.O * S;
       if (grid > INT32_MAX) return fail(ACD_ERR_UNSUPPORTED, "reduction grid too large");
       if (vec)
@@ -591,10 +591,9 @@ static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t
       unsigned int *counters = nullptr;
       if (S > 1) {
         void *scratch;
-        const size_t cbytes = align_up(sizeof(unsigned int) * ctas, 256);
-        ACD_TRY(get_scratch(ctx, cbytes + sizeof(Acc) * p.I * p.O * S, stream, &scratch));
-        counters = static_cast<unsigned int *>(scratch);
-        partials = reinterpret_cast<Acc *>(static_cast<char *>(scratch) + cbytes);
+        ACD_TRY(get_counters(ctx, (size_t)ctas, stream, &counters));
+        ACD_TRY(get_scratch(ctx, sizeof(Acc) * p.I * p.O * S, stream, &scratch));
+        partials = static_cast<Acc *>(scratch);
       }
 #define ACD_OUTER(WRV, VECV)                                                                            \
   k_red_outer<Acc, T, V, WRV, VECV><<<(int)grid, 256, 0, stream>>>(in, p.I, p.R, p.si, p.sr, p.so, p.O, S, \

@@ -293,9 +293,11 @@ struct ArgAcc {
       if (none) {
         key = LLONG_MIN;
       } else {
+        // -0 and +0 compare equal in the reduction; give them one key so the
+        // index decides between them across shards too
         uint32_t ob;
-        if constexpr (std::is_same<T, float>::value) ob = ordered_bits(v);
-        else ob = ordered_bits((float)v);
+        if constexpr (std::is_same<T, float>::value) ob = ordered_bits(v + 0.0f);
+        else ob = ordered_bits((float)v + 0.0f);
         const uint64_t gi = (uint64_t)(i + os.index_base);
         const uint64_t u = ((uint64_t)ob << 32) | (uint64_t)(0xFFFFFFFFu - (uint32_t)gi);
         key = (long long)(u ^ 0x8000000000000000ull);

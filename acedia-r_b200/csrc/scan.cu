@@ -261,16 +261,13 @@ static acd_status launch_scan(acd_ctx *ctx, ScanArgs a, cudaStream_t s) {
   a.rtiles = (a.R + RT - 1) / RT;
   a.ntiles = a.lblocks * a.O * a.rtiles;
   if (a.ntiles > 0x7fffffffLL) return fail(ACD_ERR_UNSUPPORTED, "scan: too many tiles");
-  const size_t fbytes = (size_t)a.ntiles * sizeof(uint32_t);
-  const size_t foff = 0;
-  const size_t aoff = (fbytes + 255) / 256 * 256;
   const size_t dbytes = (size_t)a.ntiles * LT * sizeof(double);
-  const size_t ioff = aoff + (dbytes + 255) / 256 * 256;
+  const size_t ioff = (dbytes + 255) / 256 * 256;
+  ACD_TRY(get_flags(ctx, (size_t)a.ntiles, s, &a.flags));
   void *scratch;
   ACD_TRY(get_scratch(ctx, ioff + dbytes, s, &scratch));
   char *base = static_cast<char *>(scratch);
-  a.flags = reinterpret_cast<uint32_t *>(base + foff);
-  a.agg = reinterpret_cast<double *>(base + aoff);
+  a.agg = reinterpret_cast<double *>(base);
   a.incl = reinterpret_cast<double *>(base + ioff);
   a.control = ctx->control;
   ctx->epoch = (ctx->epoch + 1) & 0x3fffffffu;

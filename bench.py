@@ -36,7 +36,7 @@ BYTES_PER_ELEM = {"transpose": 8, "fused_chain": 8, "stats": 4, "argmax_keys": 4
 def parse():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=10)
+    ap.add_argument("--steps", type=int, default=40)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="acediar", choices=["acediar", "reference"])
     ap.add_argument("--e2e-steps", type=int, default=2)
@@ -69,10 +69,13 @@ class Clocks:
                 ["nvidia-smi", "--query-gpu=index,clocks.sm,clocks.max.sm,power.draw,"
                  "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
                  "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap",
-                 "--format=csv,noheader,nounits", "-lms", "200"],
+                 "--format=csv,noheader,nounits", "-lms", "100"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.t = threading.Thread(target=self._read, daemon=True)
             self.t.start()
+            t0 = time.time()  # wait for the sampler's first line before timing
+            while not self.lines and time.time() - t0 < 5.0 and self.proc.poll() is None:
+                time.sleep(0.02)
         except Exception:
             self.proc = None
 

@@ -9,9 +9,11 @@
  *   - elementwise formulas of the reference functors
  *     (src/kernels/tensor_kernels.cuh:10-192): sigmoid = 1/(1+exp(-x)),
  *     relu = fmax(x, 0), round = rint, max/min = fmax/fmin, comparisons 1/0;
- *     each R operator rounds once in the tensor dtype (float ops are computed
- *     in long double and rounded once, which is correctly rounded except in
- *     rare double-rounding cases);
+ *     each R operator rounds once in the tensor dtype: + - * / and sqrt are
+ *     the native IEEE float/double operations, transcendental functions are
+ *     evaluated in long double and rounded once; sigmoid() of a float32
+ *     tensor is evaluated as base R does (in double precision or better)
+ *     and rounded once;
  *   - reductions as base R computes them: sum in a long double accumulator,
  *     mean as sum/n followed by R's correction pass mean += sum(x-mean)/n,
  *     var two-pass with divisor n-1 (the reference also divides by n-1,
@@ -92,27 +94,59 @@ static int64_t offset_of(int64_t idx, int nd, const int64_t *shape, const int64_
   return off;
 }
 
+/* correctly rounded arithmetic in the tensor dtype: float and double use the
+ * native IEEE operation (computing in long double and rounding afterwards
+ * could round twice) */
+static long double add_dt(long double a, long double b, int dt) {
+  if (dt == DT_F32) return (float)a + (float)b;
+  if (dt == DT_F64) return (double)a + (double)b;
+  return a + b;
+}
+static long double sub_dt(long double a, long double b, int dt) {
+  if (dt == DT_F32) return (float)a - (float)b;
+  if (dt == DT_F64) return (double)a - (double)b;
+  return a - b;
+}
+static long double mul_dt(long double a, long double b, int dt) {
+  if (dt == DT_F32) return (float)a * (float)b;
+  if (dt == DT_F64) return (double)a * (double)b;
+  return a * b;
+}
+static long double div_dt(long double a, long double b, int dt) {
+  if (dt == DT_F32) return (float)a / (float)b;
+  if (dt == DT_F64) return (double)a / (double)b;
+  return a / b;
+}
+static long double sqrt_dt(long double x, int dt) {
+  if (dt == DT_F32) return sqrtf((float)x);
+  if (dt == DT_F64) return sqrt((double)x);
+  return sqrtl(x);
+}
+
 static long double unary(int op, long double x, int dt) {
   switch (op) {
     case U_EXP: return rnd(expl(x), dt);
     case U_LOG: return rnd(logl(x), dt);
-    case U_SQRT: return rnd(sqrtl(x), dt);
+    case U_SQRT: return sqrt_dt(x, dt);
     case U_ABS: return fabsl(x);
     case U_FLOOR: return floorl(x);
     case U_CEIL: return ceill(x);
     case U_ROUND: return rintl(x); /* half to even, as rint */
     case U_ERF: return rnd(erfl(x), dt);
     case U_TANH: return rnd(tanhl(x), dt);
-    case U_SIGMOID: {
-      const long double e = rnd(expl(-x), dt);
-      const long double d = rnd(1.0L + e, dt);
-      return rnd(1.0L / d, dt);
-    }
+    case U_SIGMOID:
+      if (dt == DT_F64) {
+        /* base R on doubles: 1/(1+exp(-x)), one rounding per operator */
+        const long double e = rnd(expl(-x), dt);
+        return div_dt(1.0L, add_dt(1.0L, e, dt), dt);
+      }
+      /* float32 tensor: base R evaluates in double; one rounding to float */
+      return rnd(1.0L / (1.0L + expl(-x)), dt);
     case U_RELU: return isnan(x) ? 0.0L : (x > 0.0L ? x : 0.0L); /* fmax(x, 0) */
     case U_SIN: return rnd(sinl(x), dt);
     case U_COS: return rnd(cosl(x), dt);
     case U_NEG: return -x;
-    case U_SQUARE: return rnd(x * x, dt);
+    case U_SQUARE: return mul_dt(x, x, dt);
     default: return x;
   }
 }
@@ -130,21 +164,21 @@ static long double fminl_r(long double a, long double b) {
 
 static long double binary(int op, long double a, long double b, int dt) {
   switch (op) {
-    case B_ADD: return rnd(a + b, dt);
-    case B_SUB: return rnd(a - b, dt);
-    case B_MUL: return rnd(a * b, dt);
-    case B_DIV: return rnd(a / b, dt);
+    case B_ADD: return add_dt(a, b, dt);
+    case B_SUB: return sub_dt(a, b, dt);
+    case B_MUL: return mul_dt(a, b, dt);
+    case B_DIV: return div_dt(a, b, dt);
     case B_MAX: return fmaxl_r(a, b);
     case B_MIN: return fminl_r(a, b);
-    case B_POW: return (b == 2.0L) ? rnd(a * a, dt) : rnd(powl(a, b), dt);
+    case B_POW: return (b == 2.0L) ? mul_dt(a, a, dt) : rnd(powl(a, b), dt);
     case B_GT: return a > b;
     case B_LT: return a < b;
     case B_EQ: return a == b;
     case B_NE: return a != b;
     case B_GE: return a >= b;
     case B_LE: return a <= b;
-    case B_RSUB: return rnd(b - a, dt);
-    case B_RDIV: return rnd(b / a, dt);
+    case B_RSUB: return sub_dt(b, a, dt);
+    case B_RDIV: return div_dt(b, a, dt);
   }
   return 0.0L;
 }
@@ -181,10 +215,10 @@ void orc_gauss_chain(int dt, const void *in, int64_t n, double p, void *out) {
   const long double pv = rnd(p, dt);
   for (int64_t i = 0; i < n; ++i) {
     const long double x = ld_get(in, dt, i);
-    const long double a = rnd(x * pv, dt);
-    const long double sq = rnd(x * x, dt);
+    const long double a = mul_dt(x, pv, dt);
+    const long double sq = mul_dt(x, x, dt);
     const long double e = rnd(expl(-sq), dt);
-    put(out, dt, i, rnd(a + e, dt));
+    put(out, dt, i, add_dt(a, e, dt));
   }
 }
 
