@@ -265,6 +265,21 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
+// Blocks of `kernel` resident per SM at `threads` threads and `smem` dynamic
+// shared memory (occupancy API, cached per kernel and launch shape).
+int resident_blocks(const void *kernel, int threads, size_t smem);
+
+// Persistent grid: as many blocks as are resident at once (a multiple of the
+// SM count), or fewer when there is less work.  A larger grid would run as a
+// second, partly filled wave.
+template <typename K>
+inline int persistent_grid(const acd_ctx *ctx, K kernel, int threads, size_t smem, int64_t work_blocks) {
+  const int nb = resident_blocks(reinterpret_cast<const void *>(kernel), threads, smem);
+  int64_t cap = (int64_t)ctx->sm_count * nb;
+  if (work_blocks < cap) cap = work_blocks;
+  return cap < 1 ? 1 : (int)cap;
+}
+
 // Grid sizing: a multiple of the SM count.
 inline int grid_for(const acd_ctx *ctx, int64_t work_items, int per_block, int blocks_per_sm) {
   int64_t want = (work_items + per_block - 1) / per_block;

@@ -97,6 +97,32 @@ static acd_status get_zeroed(acd_ctx *ctx, W **region, size_t *have, size_t n, c
   return ACD_OK;
 }
 
+int resident_blocks(const void *kernel, int threads, size_t smem) {
+  struct Key {
+    const void *k;
+    int t;
+    size_t s;
+  };
+  static std::mutex mu;
+  static Key keys[256];
+  static int vals[256];
+  static int used = 0;
+  std::lock_guard<std::mutex> lk(mu);
+  for (int i = 0; i < used; ++i)
+    if (keys[i].k == kernel && keys[i].t == threads && keys[i].s == smem) return vals[i];
+  int nb = 0;
+  if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kernel, threads, smem) != cudaSuccess || nb < 1) {
+    cudaGetLastError();
+    nb = 1;
+  }
+  if (used < 256) {
+    keys[used] = Key{kernel, threads, smem};
+    vals[used] = nb;
+    ++used;
+  }
+  return nb;
+}
+
 acd_status get_counters(acd_ctx *ctx, size_t n, cudaStream_t stream, unsigned int **out) {
   ACD_TRY(get_zeroed(ctx, &ctx->counters, &ctx->counters_n, n, stream, "counter"));
   *out = ctx->counters;

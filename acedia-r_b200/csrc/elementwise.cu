@@ -197,7 +197,7 @@ __global__ void __launch_bounds__(kEwThreads) k_general(typename F::Out *__restr
 // which concentrates the traffic on a few memory channels).  Full tiles with
 // aligned rows use 16-byte loads and stores.
 template <typename T, int TILE>
-__global__ void __launch_bounds__(256) k_transpose(T *__restrict__ out, const T *__restrict__ in, int64_t n0,
+__global__ void __launch_bounds__(256, 8) k_transpose(T *__restrict__ out, const T *__restrict__ in, int64_t n0,
                                                    int64_t n1, int64_t n2, int64_t os1, int64_t os2, int64_t is0,
                                                    int64_t is2, int64_t tiles0, int64_t tiles1, int vec_ok) {
   constexpr int V = (sizeof(T) >= 4) ? 16 / (int)sizeof(T) : 1;
@@ -280,7 +280,8 @@ static acd_status launch_map(acd_ctx *ctx, const F &f, const acd_desc *out, cons
     const bool ok = aligned_to<T>(pa, sizeof(T)) && aligned_to<O>(po, sizeof(O)) && ca == co && cb == ca;
     const int64_t head = ok ? (V - ca) % V : n;
     const int64_t head_c = head > n ? n : head;
-    const int grid = grid_for(ctx, ok ? (n - head_c) / V + 1 : n, kEwThreads * 2, 8);
+    const int64_t work = ((ok ? (n - head_c) / V + 1 : n) + kEwThreads * 2 - 1) / (kEwThreads * 2);
+    const int grid = persistent_grid(ctx, k_flat<F, V, 2>, kEwThreads, 0, work);
     k_flat<F, V, 2><<<grid, kEwThreads, 0, stream>>>(po, pa, pb, n, head_c, f);
     return ACD_OK;
   }
@@ -300,10 +301,12 @@ static acd_status launch_map(acd_ctx *ctx, const F &f, const acd_desc *out, cons
     if (ok) {
       const int64_t nv0 = n0 / V;
       const int64_t total = nv0 * n1;
-      const int grid = grid_for(ctx, total, kEwThreads, 8);
+      const int64_t work = (total + kEwThreads - 1) / kEwThreads;
       if (total < (1ll << 32) && nv0 < (1ll << 31)) {
+        const int grid = persistent_grid(ctx, k_rows<F, V, true>, kEwThreads, 0, work);
         k_rows<F, V, true><<<grid, kEwThreads, 0, stream>>>(po, os1, A, B, nv0, n1, FastDiv((uint32_t)nv0), f);
       } else {
+        const int grid = persistent_grid(ctx, k_rows<F, V, false>, kEwThreads, 0, work);
         k_rows<F, V, false><<<grid, kEwThreads, 0, stream>>>(po, os1, A, B, nv0, n1, FastDiv(1), f);
       }
       return ACD_OK;
@@ -317,7 +320,7 @@ static acd_status launch_map(acd_ctx *ctx, const F &f, const acd_desc *out, cons
     g.shape[d] = d < it.ndim ? it.shape[d] : 1;
     for (int o = 0; o < kMaxOps; ++o) g.st[o][d] = (d < it.ndim && o < it.nops) ? it.stride[o][d] : 0;
   }
-  const int grid = grid_for(ctx, (n + 3) / 4, kEwThreads, 8);
+  const int grid = persistent_grid(ctx, k_general<F, 4>, kEwThreads, 0, ((n + 3) / 4 + kEwThreads - 1) / kEwThreads);
   k_general<F, 4><<<grid, kEwThreads, 0, stream>>>(po, pa, pb, g, n, f);
   return ACD_OK;
 }
@@ -328,7 +331,14 @@ static void launch_transpose(acd_ctx *ctx, T *out, const T *in, int64_t n0, int6
   constexpr int V = (sizeof(T) >= 4) ? 16 / (int)sizeof(T) : 1;
   const int64_t tiles0 = (n0 + TILE - 1) / TILE, tiles1 = (n1 + TILE - 1) / TILE;
   const int64_t ntiles = tiles0 * tiles1 * n2;
-  const int grid = grid_for(ctx, ntiles, 1, 8);
+  static bool carveout_set = false;  // one shared-memory carveout request per instantiation
+  if (!carveout_set) {
+    cudaFuncSetAttribute(k_transpose<T, TILE>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                         cudaSharedmemCarveoutMaxShared);
+    cudaGetLastError();
+    carveout_set = true;
+  }
+  const int grid = persistent_grid(ctx, k_transpose<T, TILE>, 256, 0, ntiles);
   const int vec_ok = V > 1 && is0 % V == 0 && os1 % V == 0 && is2 % V == 0 && os2 % V == 0 &&
                      aligned_to<T>(in, 16) && aligned_to<T>(out, 16);
   k_transpose<T, TILE><<<grid, 256, 0, stream>>>(out, in, n0, n1, n2, os1, os2, is0, is2, tiles0, tiles1, vec_ok);

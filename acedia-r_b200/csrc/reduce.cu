@@ -518,9 +518,11 @@ static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t
       if (p.n == 0) return fail(ACD_ERR_UNSUPPORTED, "reduction of an empty tensor");
       int grid;
       if (p.kind == Plan::kFullFlat)
-        grid = grid_for(ctx, (p.n + V - 1) / V, kRedThreads * 4, 2);
+        grid = persistent_grid(ctx, k_red_flat<Acc, T, V, 4>, kRedThreads, 0,
+                               ((p.n + V - 1) / V + kRedThreads * 4 - 1) / (kRedThreads * 4));
       else
-        grid = grid_for(ctx, (p.n + 3) / 4, kRedThreads, 2);
+        grid = persistent_grid(ctx, k_red_strided<Acc, T>, kRedThreads, 0,
+                               ((p.n + 3) / 4 + kRedThreads - 1) / kRedThreads);
       void *scratch;
       ACD_TRY(get_scratch(ctx, align_up(sizeof(Acc) * grid, 256), stream, &scratch));
       Acc *partials = static_cast<Acc *>(scratch);
@@ -542,11 +544,14 @@ static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t
       const int64_t warps_wanted = p.O;
       const int64_t target_threads = (int64_t)ctx->sm_count * 2048;
       if (p.O * 32 >= target_threads / 2 || p.R <= 4096) {
-        const int grid = grid_for(ctx, warps_wanted * 32, 256, 8);
-        if (vec)
+        const int64_t work = (warps_wanted * 32 + 255) / 256;
+        if (vec) {
+          const int grid = persistent_grid(ctx, k_red_inner_warp<Acc, T, V, true>, 256, 0, work);
           k_red_inner_warp<Acc, T, V, true><<<grid, 256, 0, stream>>>(in, p.R, p.sr, p.so, p.O, os);
-        else
+        } else {
+          const int grid = persistent_grid(ctx, k_red_inner_warp<Acc, T, V, false>, 256, 0, work);
           k_red_inner_warp<Acc, T, V, false><<<grid, 256, 0, stream>>>(in, p.R, p.sr, p.so, p.O, os);
+        }
         return ACD_OK;
       }
       // few long fibers: split each over S CTAs
@@ -608,7 +613,7 @@ static acd_status run_plan(acd_ctx *ctx, const Plan &p, OutSpec os, cudaStream_t
     }
     case Plan::kGeneric: {
       os.n = p.R;
-      const int grid = grid_for(ctx, p.O * 32, 256, 8);
+      const int grid = persistent_grid(ctx, k_red_generic<Acc, T>, 256, 0, (p.O * 32 + 255) / 256);
       k_red_generic<Acc, T><<<grid, 256, 0, stream>>>(in, p.ax, p.O, p.R, os);
       return ACD_OK;
     }
