@@ -196,6 +196,17 @@ acd_status acd_scan(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_des
 acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, int32_t axis,
                        acd_stream stream);
 
+/* Cumulative sum/product exactly as acd_scan, for callers that cannot
+ * allocate device memory (no context, no workspace): the scratch is a static
+ * 8 MiB device array held by every GPU that loads this library.  Problems
+ * whose scratch would not fit (about 1.7e9 elements along a contiguous axis,
+ * 1.3e8 with interleaved float32 lanes) return ACD_ERR_UNSUPPORTED.  Runs on
+ * the current device; the first call on a device looks up the array's device
+ * address, so make it before any stream capture.  Calls that overlap on the
+ * GPU race on the shared array.  This entry point has no counterpart in the
+ * reference. */
+acd_status acd_scan_noalloc(int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis, acd_stream stream);
+
 /* ---- sharded partials (multi-GPU global sum/var and argmax) ------------- */
 /* Writes this shard's partial statistics of all elements of `in` to the
  * device array `stats` (float64[4]: n, shift, sum(x-shift), sum((x-shift)^2)),
