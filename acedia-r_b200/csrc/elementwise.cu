@@ -245,6 +245,38 @@ __global__ void __launch_bounds__(256, 8) k_transpose(T *__restrict__ out, const
   }
 }
 
+// The same transpose when every tile is full, rows are 16-byte aligned and
+// there is no batch axis (the permute -> contiguous of a dense 3-D tensor
+// collapses to this): no bounds checks, no scalar path, 16-byte accesses only.
+template <typename T, int TILE>
+__global__ void __launch_bounds__(256) k_transpose_full(T *__restrict__ out, const T *__restrict__ in, int64_t n0,
+                                                        int64_t n1, int64_t os1, int64_t is0, int64_t tiles0,
+                                                        int64_t tiles1) {
+  constexpr int V = 16 / (int)sizeof(T);
+  __shared__ T tile[TILE][TILE + 1];
+  const int64_t nt = tiles0 * tiles1;
+  for (int64_t t = blockIdx.x; t < nt; t += gridDim.x) {
+    const int64_t ti = t % tiles0;
+    const int64_t tj = (t / tiles0 + ti) % tiles1;
+    const int64_t i0 = ti * TILE, j0 = tj * TILE;
+    for (int e = threadIdx.x; e < TILE * (TILE / V); e += blockDim.x) {
+      const int r = e / (TILE / V), cv = e % (TILE / V);
+      const Vec<T, V> x = *reinterpret_cast<const Vec<T, V> *>(in + (i0 + r) * is0 + j0 + cv * V);
+#pragma unroll
+      for (int q = 0; q < V; ++q) tile[r][cv * V + q] = x.v[q];
+    }
+    __syncthreads();
+    for (int e = threadIdx.x; e < TILE * (TILE / V); e += blockDim.x) {
+      const int r = e / (TILE / V), cv = e % (TILE / V);
+      Vec<T, V> y;
+#pragma unroll
+      for (int q = 0; q < V; ++q) y.v[q] = tile[cv * V + q][r];
+      *reinterpret_cast<Vec<T, V> *>(out + (i0 + cv * V) + (j0 + r) * os1) = y;
+    }
+    __syncthreads();
+  }
+}
+
 // ---------------------------------------------------------------------------
 // launch selection
 // ---------------------------------------------------------------------------
@@ -341,6 +373,20 @@ static void launch_transpose(acd_ctx *ctx, T *out, const T *in, int64_t n0, int6
   const int grid = persistent_grid(ctx, k_transpose<T, TILE>, 256, 0, ntiles);
   const int vec_ok = V > 1 && is0 % V == 0 && os1 % V == 0 && is2 % V == 0 && os2 % V == 0 &&
                      aligned_to<T>(in, 16) && aligned_to<T>(out, 16);
+  if constexpr (V > 1) {
+    if (vec_ok && n2 == 1 && n0 % TILE == 0 && n1 % TILE == 0) {
+      static bool full_carveout_set = false;
+      if (!full_carveout_set) {
+        cudaFuncSetAttribute(k_transpose_full<T, TILE>, cudaFuncAttributePreferredSharedMemoryCarveout,
+                             cudaSharedmemCarveoutMaxShared);
+        cudaGetLastError();
+        full_carveout_set = true;
+      }
+      const int g2 = persistent_grid(ctx, k_transpose_full<T, TILE>, 256, 0, ntiles);
+      k_transpose_full<T, TILE><<<g2, 256, 0, stream>>>(out, in, n0, n1, os1, is0, tiles0, tiles1);
+      return;
+    }
+  }
   k_transpose<T, TILE><<<grid, 256, 0, stream>>>(out, in, n0, n1, n2, os1, os2, is0, is2, tiles0, tiles1, vec_ok);
 }
 

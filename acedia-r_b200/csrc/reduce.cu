@@ -90,22 +90,37 @@ __global__ void __launch_bounds__(kRedThreads) k_red_flat(const T *__restrict__ 
     acc.add(in[e], e);
   }
   const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(in + head);
-  for (int64_t v0 = tid; v0 < nvec; v0 += nth * U) {
+  // one accumulator per vector in flight: no dependency chain links the U
+  // loads of an iteration, so they stay in flight together
+  Acc part[U];
+#pragma unroll
+  for (int u = 0; u < U; ++u) {
+    part[u].init();
+    if constexpr (Acc::kShift) part[u].set_shift(K);
+  }
+  // main loop: U full vectors per thread, no guards, so all U loads are
+  // issued before any is consumed
+  int64_t v0 = tid;
+  for (; v0 + (int64_t)(U - 1) * nth < nvec; v0 += nth * U) {
     Vec<T, V> x[U];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t v = v0 + (int64_t)u * nth;
-      if (v < nvec) x[u] = pv[v];
-    }
+    for (int u = 0; u < U; ++u) x[u] = pv[v0 + (int64_t)u * nth];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
       const int64_t v = v0 + (int64_t)u * nth;
-      if (v < nvec) {
 #pragma unroll
-        for (int k = 0; k < V; ++k) acc.add(x[u].v[k], head + v * V + k);
-      }
+      for (int k = 0; k < V; ++k) part[u].add(x[u].v[k], head + v * V + k);
     }
   }
+  // remainder: fewer than U vectors left for this thread
+  for (int u = 0; v0 + (int64_t)u * nth < nvec; ++u) {
+    const int64_t v = v0 + (int64_t)u * nth;
+    const Vec<T, V> x = pv[v];
+#pragma unroll
+    for (int k = 0; k < V; ++k) part[0].add(x.v[k], head + v * V + k);
+  }
+#pragma unroll
+  for (int u = 0; u < U; ++u) acc.merge(part[u]);
   finish_grid(acc, smem, partials, counter, os, 0, K);
 }
 
@@ -287,7 +302,21 @@ __global__ void __launch_bounds__(256) k_red_outer(const T *__restrict__ in, int
     }
   }
   const bool full = VEC && (i0 + V <= I);
-  for (int64_t r = r0 + wr; r < r1; r += WR) {
+  int64_t r = r0 + wr;
+  if (full) {
+    // four rows in flight per thread; accumulation stays in row order
+    for (; r + 3 * WR < r1; r += 4 * WR) {
+      Vec<T, V> x[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const Vec<T, V> *>(base + (r + u * WR) * sr + i0);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+#pragma unroll
+        for (int k = 0; k < V; ++k) acc[k].add(x[u].v[k], r + u * WR);
+      }
+    }
+  }
+  for (; r < r1; r += WR) {
     const T *row = base + r * sr;
     if (full) {
       const Vec<T, V> x = *reinterpret_cast<const Vec<T, V> *>(row + i0);

@@ -38,12 +38,13 @@ __device__ __forceinline__ uint32_t load_flag(const uint32_t *p) {
 // Thread layout: LT lanes x G step groups (LT * G == 256).  Each thread scans
 // SEG consecutive steps of one lane in registers.
 template <typename T, bool PROD, int LT, int SEG>
-__global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
+__global__ void __launch_bounds__(256, 3) k_scan(ScanArgs a) {
   constexpr int G = 256 / LT;
   constexpr int RT = G * SEG;  // steps per tile
   __shared__ int64_t s_tile;
   __shared__ double s_tot[G][LT];
   __shared__ double s_prefix[LT];
+  __shared__ double s_win[LT > 1 ? 32 : 1][LT];
   const double ident = PROD ? 1.0 : 0.0;
 
   if (threadIdx.x == 0) s_tile = (int64_t)atomicAdd(&a.control->counters[1], 1u);
@@ -60,17 +61,17 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
   const T *in = static_cast<const T *>(a.in) + o * a.so + (lane_ok ? l : 0) * a.sl;
   T *out = static_cast<T *>(a.out) + o * a.oo + (lane_ok ? l : 0) * a.ol;
 
-  // 1. load and scan this thread's segment
-  double v[SEG];
-  double run = ident;
+  // 1. load this thread's segment (kept in the tensor dtype, so a thread
+  // holds SEG values of T rather than SEG doubles) and reduce it in double
+  T xs[SEG];
 #pragma unroll
   for (int k = 0; k < SEG; ++k) {
     const int64_t r = r0 + k;
-    double x = ident;
-    if (lane_ok && r < a.R) x = (double)in[r * a.sr];
-    run = combine<PROD>(run, x);
-    v[k] = run;
+    xs[k] = (lane_ok && r < a.R) ? in[r * a.sr] : T(PROD ? 1 : 0);
   }
+  double run = ident;
+#pragma unroll
+  for (int k = 0; k < SEG; ++k) run = combine<PROD>(run, (double)xs[k]);
 
   // 2. exclusive prefix of the segment totals within the tile, per lane
   double excl = ident;
@@ -109,12 +110,15 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
     tile_total = all;
   }
 
-  // 3. publish and look back (warp 0, one data lane per thread lane)
+  // 3. publish and look back (warp 0).  Data lane dl < LT is carried by
+  // thread dl (threads 0..LT-1 form step group 0); for LT == 1 the tile total
+  // is uniform across threads.  The look-back inspects a window of 32
+  // predecessors at once: lane l waits (bounded) for predecessor base - l to
+  // publish, a ballot finds the nearest inclusive prefix, and the window's
+  // aggregates are added in tile order.
   if (threadIdx.x < 32) {
     const int dl = threadIdx.x;
     const uint32_t ep = a.epoch << 2;
-    // Thread dl < LT of warp 0 carries data lane dl (threads 0..LT-1 form
-    // step group 0); for LT == 1 the tile total is uniform across threads.
     const double my_total = tile_total;
     const bool publish = (tile != a.fault_tile);
     double prefix = ident;
@@ -132,18 +136,20 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
         __syncwarp();
         if (dl == 0) atomicExch(&a.flags[tile], ep | kFlagAgg);
       }
-      int64_t j = tile - 1;
+      const int64_t chain_start = tile - q;
+      int64_t base = tile - 1;
       while (true) {
-        // lane 0 waits (bounded) and broadcasts, so control stays warp-uniform
+        const int64_t p = base - dl;
+        const bool valid = p >= chain_start;
         uint32_t f = 0u;
         int gave_up = 0;
-        if (dl == 0) {
-          f = load_flag(&a.flags[j]);
+        if (valid) {
+          f = load_flag(&a.flags[p]);
           if ((f & ~3u) != ep || (f & 3u) == 0u) {
             const uint64_t t0 = global_timer_ns();
             uint32_t spins = 0;
             while (true) {
-              f = load_flag(&a.flags[j]);
+              f = load_flag(&a.flags[p]);
               if ((f & ~3u) == ep && (f & 3u) != 0u) break;
               if (load_flag(&a.control->scan_abort) == a.epoch) { gave_up = 1; break; }
               if ((int64_t)(global_timer_ns() - t0) > a.timeout_ns || ++spins > (1u << 26)) {
@@ -152,19 +158,47 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
                 atomicExch(&a.control->scan_abort, a.epoch);
                 break;
               }
-              __nanosleep(64);
+              __nanosleep(32);
             }
           }
         }
-        f = __shfl_sync(0xffffffffu, f, 0);
-        gave_up = __shfl_sync(0xffffffffu, gave_up, 0);
-        if (gave_up) break;
+        if (__any_sync(0xffffffffu, gave_up)) break;
         __threadfence();
-        const bool inc = (f & 3u) == kFlagIncl;
-        const double pv = (dl < LT) ? __ldcg(inc ? &a.incl[j * LT + dl] : &a.agg[j * LT + dl]) : ident;
-        prefix = combine<PROD>(pv, prefix);
-        if (inc) break;
-        --j;
+        const unsigned incl = __ballot_sync(0xffffffffu, valid && (f & 3u) == kFlagIncl);
+        // lanes 0..stop contribute: aggregates before the nearest inclusive
+        // prefix, then the inclusive prefix itself (the chain's first tile
+        // always publishes one, so a window that reaches it stops there)
+        const int stop = incl ? __ffs(incl) - 1 : 31;
+        if constexpr (LT == 1) {
+          double v = ident;
+          if (dl <= stop && valid) v = __ldcg(((f & 3u) == kFlagIncl) ? &a.incl[p] : &a.agg[p]);
+          // combine in tile order: lane stop is the oldest
+#pragma unroll
+          for (int d = 16; d > 0; d >>= 1) {
+            const double o = __shfl_down_sync(0xffffffffu, v, d);
+            if (dl + d < 32) v = combine<PROD>(v, o);
+          }
+          v = __shfl_sync(0xffffffffu, v, 0);
+          prefix = combine<PROD>(v, prefix);
+        } else {
+          // stage the window's values with independent loads, then combine
+          // them in tile order (oldest first)
+#pragma unroll 8
+          for (int l = 0; l < 32; ++l) {
+            if (l <= stop && dl < LT) {
+              const int64_t pl = base - l;
+              s_win[l][dl] = __ldcg(((incl >> l) & 1u) ? &a.incl[pl * LT + dl] : &a.agg[pl * LT + dl]);
+            }
+          }
+          __syncwarp();
+          double w = ident;
+          for (int l = stop; l >= 0; --l)
+            if (dl < LT) w = combine<PROD>(w, s_win[l][dl]);
+          __syncwarp();
+          prefix = combine<PROD>(w, prefix);
+        }
+        if (incl) break;
+        base -= 32;
       }
       // publish the inclusive prefix (also after giving up, so that later
       // tiles never wait on this one)
@@ -179,12 +213,14 @@ __global__ void __launch_bounds__(256) k_scan(ScanArgs a) {
   }
   __syncthreads();
 
-  // 4. write outputs
-  const double base = combine<PROD>(s_prefix[lane], excl);
+  // 4. write outputs: the running value restarts from the tile prefix and
+  // this segment's exclusive prefix
+  double acc = combine<PROD>(s_prefix[lane], excl);
 #pragma unroll
   for (int k = 0; k < SEG; ++k) {
     const int64_t r = r0 + k;
-    if (lane_ok && r < a.R) out[r * a.orr] = (T)combine<PROD>(base, v[k]);
+    acc = combine<PROD>(acc, (double)xs[k]);
+    if (lane_ok && r < a.R) out[r * a.orr] = (T)acc;
   }
 
   // 5. the last CTA to finish resets the ticket counters

@@ -65,6 +65,7 @@ __global__ void __launch_bounds__(256) k_softmax_axis(SoftArgs a) {
 
   // pass 1: load (into shared memory where it fits) and take the lane maximum
   T m = lowest_of<T>();
+#pragma unroll 8
   for (int64_t r = r0 + grp; r < r1; r += G) {
     T x = lowest_of<T>();
     if (lane_ok) x = in[r * a.sr];
@@ -90,6 +91,7 @@ __global__ void __launch_bounds__(256) k_softmax_axis(SoftArgs a) {
 
   // pass 2: e = exp(x - M), kept in shared memory; lane sums in float64
   double s = 0.0;
+#pragma unroll 8
   for (int64_t r = r0 + grp; r < r1; r += G) {
     const int64_t k = r - r0;
     T x;
@@ -120,6 +122,7 @@ __global__ void __launch_bounds__(256) k_softmax_axis(SoftArgs a) {
 
   // pass 3: write
   if (lane_ok) {
+#pragma unroll 8
     for (int64_t r = r0 + grp; r < r1; r += G) {
       const int64_t k = r - r0;
       T e;
@@ -130,6 +133,239 @@ __global__ void __launch_bounds__(256) k_softmax_axis(SoftArgs a) {
       out[r * a.orr] = e * inv;
     }
   }
+}
+
+// ---- two passes, for rows whose chunk does not fit shared memory -----------
+// Pass 1: each CTA reduces LT lanes x `chunk` steps to per-lane online
+// (max, sum of exp(x - max)) partials.  Pass 2: each CTA merges the partials
+// of its lanes over all chunks, then re-reads its chunk and writes the
+// normalised values.  Reads each element twice, writes it once; every CTA is
+// independent, so occupancy is not limited by a cluster or by shared memory.
+template <typename T, int LT>
+__global__ void __launch_bounds__(256) k_softmax_partials(SoftArgs a, int64_t nchunks, double2 *__restrict__ part) {
+  constexpr int G = 256 / LT;
+  __shared__ double2 red[G][LT];
+  const int64_t c = blockIdx.x % nchunks, gid = blockIdx.x / nchunks;
+  const int64_t o = gid / a.lblocks, lb = gid % a.lblocks;
+  const int lane = (LT == 1) ? 0 : (int)(threadIdx.x % LT);
+  const int grp = (LT == 1) ? (int)threadIdx.x : (int)(threadIdx.x / LT);
+  const int64_t l = lb * LT + lane;
+  const bool lane_ok = l < a.L;
+  const int64_t r0 = c * a.chunk;
+  int64_t r1 = r0 + a.chunk;
+  if (r1 > a.R) r1 = a.R;
+  const T *in = static_cast<const T *>(a.in) + o * a.so + (lane_ok ? l : 0) * a.sl;
+  double m = -INFINITY, sum = 0.0;
+  if (lane_ok) {
+#pragma unroll 8
+    for (int64_t r = r0 + grp; r < r1; r += G) {
+      const double x = (double)in[r * a.sr];
+      if (x > m) {
+        sum = sum * exp(m - x) + 1.0;
+        m = x;
+      } else if (x != -INFINITY) {
+        sum += (double)m_exp((T)(x - m));
+      }
+    }
+  }
+  red[grp][lane] = make_double2(m, sum);
+  __syncthreads();
+  if (grp == 0) {
+    double M = -INFINITY, S = 0.0;
+    for (int g = 0; g < G; ++g) {
+      const double2 v = red[g][lane];
+      if (v.x == -INFINITY) continue;
+      if (v.x > M) {
+        S = S * exp(M - v.x) + v.y;
+        M = v.x;
+      } else {
+        S += v.y * exp(v.x - M);
+      }
+    }
+    part[(gid * nchunks + c) * LT + lane] = make_double2(M, S);
+  }
+}
+
+template <typename T, int LT>
+__global__ void __launch_bounds__(256) k_softmax_finish(SoftArgs a, int64_t nchunks,
+                                                        const double2 *__restrict__ part) {
+  constexpr int G = 256 / LT;
+  __shared__ double sM[LT], sInv[LT];
+  const int64_t c = blockIdx.x % nchunks, gid = blockIdx.x / nchunks;
+  const int64_t o = gid / a.lblocks, lb = gid % a.lblocks;
+  const int lane = (LT == 1) ? 0 : (int)(threadIdx.x % LT);
+  const int grp = (LT == 1) ? (int)threadIdx.x : (int)(threadIdx.x / LT);
+  const int64_t l = lb * LT + lane;
+  const bool lane_ok = l < a.L;
+  if (grp == 0) {
+    double M = -INFINITY, S = 0.0;
+    for (int64_t q = 0; q < nchunks; ++q) {
+      const double2 v = part[(gid * nchunks + q) * LT + lane];
+      if (v.x == -INFINITY) continue;
+      if (v.x > M) {
+        S = S * exp(M - v.x) + v.y;
+        M = v.x;
+      } else {
+        S += v.y * exp(v.x - M);
+      }
+    }
+    sM[lane] = M;
+    sInv[lane] = 1.0 / S;
+  }
+  __syncthreads();
+  if (!lane_ok) return;
+  const T Mt = (T)sM[lane];
+  const T inv = (T)sInv[lane];
+  const int64_t r0 = c * a.chunk;
+  int64_t r1 = r0 + a.chunk;
+  if (r1 > a.R) r1 = a.R;
+  const T *in = static_cast<const T *>(a.in) + o * a.so + l * a.sl;
+  T *out = static_cast<T *>(a.out) + o * a.oo + l * a.ol;
+#pragma unroll 8
+  for (int64_t r = r0 + grp; r < r1; r += G) out[r * a.orr] = m_exp(in[r * a.sr] - Mt) * inv;
+}
+
+// ---- two passes over wide, contiguous lane blocks ---------------------------
+// For a softmax along a strided axis whose lanes are contiguous (the row
+// softmax of a column-major matrix): each thread owns VL adjacent lanes read
+// with one 16-byte load per step, a CTA owns 256*VL lanes, so every step of
+// the chunk is a 4 KB contiguous read.  Pass 1 writes per-lane online (max,
+// sum) partials per chunk; pass 2 merges them and writes exp(x - max) / sum.
+template <typename T>
+__device__ __forceinline__ void online_add(double &m, double &s, T x) {
+  const double xd = (double)x;
+  if (xd > m) {
+    s = s * exp(m - xd) + 1.0;
+    m = xd;
+  } else if (xd != -INFINITY) {
+    s += (double)m_exp((T)(xd - m));
+  }
+}
+
+template <typename T, int VL>
+__global__ void __launch_bounds__(256) k_softmax_wide_partials(SoftArgs a, int64_t nchunks, int64_t lblocks,
+                                                               double2 *__restrict__ part) {
+  const int64_t c = blockIdx.x % nchunks, gid = blockIdx.x / nchunks;
+  const int64_t o = gid / lblocks, lb = gid % lblocks;
+  const int64_t l0 = (lb * 256 + threadIdx.x) * VL;
+  if (l0 >= a.L) return;
+  const int64_t r0 = c * a.chunk;
+  int64_t r1 = r0 + a.chunk;
+  if (r1 > a.R) r1 = a.R;
+  const T *in = static_cast<const T *>(a.in) + o * a.so + l0;
+  // online (max, sum) in the tensor dtype, four steps at a time: one rescale
+  // exp per batch and one exp per element, no divergent branches
+  T m[VL], s[VL];
+#pragma unroll
+  for (int k = 0; k < VL; ++k) {
+    m[k] = lowest_of<T>();
+    s[k] = T(0);
+  }
+  int64_t r = r0;
+  for (; r + 3 < r1; r += 4) {
+    Vec<T, VL> x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const Vec<T, VL> *>(in + (r + u) * a.sr);
+#pragma unroll
+    for (int k = 0; k < VL; ++k) {
+      const T mb = m_max(m_max(x[0].v[k], x[1].v[k]), m_max(x[2].v[k], x[3].v[k]));
+      const T mn = m_max(m[k], mb);
+      if (mn == lowest_of<T>()) continue;  // all -inf so far
+      T acc = (m[k] == lowest_of<T>()) ? T(0) : s[k] * m_exp(m[k] - mn);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) acc += m_exp(x[u].v[k] - mn);
+      s[k] = acc;
+      m[k] = mn;
+    }
+  }
+  for (; r < r1; ++r) {
+    const Vec<T, VL> x = *reinterpret_cast<const Vec<T, VL> *>(in + r * a.sr);
+#pragma unroll
+    for (int k = 0; k < VL; ++k) {
+      const T mn = m_max(m[k], x.v[k]);
+      if (mn == lowest_of<T>()) continue;
+      const T acc = (m[k] == lowest_of<T>()) ? T(0) : s[k] * m_exp(m[k] - mn);
+      s[k] = acc + m_exp(x.v[k] - mn);
+      m[k] = mn;
+    }
+  }
+  double2 *dst = part + (gid * nchunks + c) * (int64_t)(256 * VL) + threadIdx.x * VL;
+#pragma unroll
+  for (int k = 0; k < VL; ++k)
+    dst[k] = make_double2(m[k] == lowest_of<T>() ? -INFINITY : (double)m[k], (double)s[k]);
+}
+
+template <typename T, int VL>
+__global__ void __launch_bounds__(256) k_softmax_wide_finish(SoftArgs a, int64_t nchunks, int64_t lblocks,
+                                                             const double2 *__restrict__ part) {
+  const int64_t c = blockIdx.x % nchunks, gid = blockIdx.x / nchunks;
+  const int64_t o = gid / lblocks, lb = gid % lblocks;
+  const int64_t l0 = (lb * 256 + threadIdx.x) * VL;
+  if (l0 >= a.L) return;
+  T M[VL], inv[VL];
+#pragma unroll
+  for (int k = 0; k < VL; ++k) {
+    double mm = -INFINITY, ss = 0.0;
+    for (int64_t q = 0; q < nchunks; ++q) {
+      const double2 v = part[(gid * nchunks + q) * (int64_t)(256 * VL) + threadIdx.x * VL + k];
+      if (v.x == -INFINITY) continue;
+      if (v.x > mm) {
+        ss = ss * exp(mm - v.x) + v.y;
+        mm = v.x;
+      } else {
+        ss += v.y * exp(v.x - mm);
+      }
+    }
+    M[k] = (T)mm;
+    inv[k] = (T)(1.0 / ss);
+  }
+  const int64_t r0 = c * a.chunk;
+  int64_t r1 = r0 + a.chunk;
+  if (r1 > a.R) r1 = a.R;
+  const T *in = static_cast<const T *>(a.in) + o * a.so + l0;
+  T *out = static_cast<T *>(a.out) + o * a.oo + l0;
+  int64_t r = r0;
+  for (; r + 3 < r1; r += 4) {
+    Vec<T, VL> x[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) x[u] = *reinterpret_cast<const Vec<T, VL> *>(in + (r + u) * a.sr);
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      Vec<T, VL> y;
+#pragma unroll
+      for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x[u].v[k] - M[k]) * inv[k];
+      *reinterpret_cast<Vec<T, VL> *>(out + (r + u) * a.orr) = y;
+    }
+  }
+  for (; r < r1; ++r) {
+    const Vec<T, VL> x = *reinterpret_cast<const Vec<T, VL> *>(in + r * a.sr);
+    Vec<T, VL> y;
+#pragma unroll
+    for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x.v[k] - M[k]) * inv[k];
+    *reinterpret_cast<Vec<T, VL> *>(out + r * a.orr) = y;
+  }
+}
+
+template <typename T>
+static acd_status launch_softmax_wide(acd_ctx *ctx, SoftArgs a, cudaStream_t s) {
+  constexpr int VL = 16 / sizeof(T);
+  const int64_t lblocks = (a.L + 256 * VL - 1) / (256 * VL);
+  const int64_t groups = lblocks * a.O;
+  int64_t nchunks = ((int64_t)ctx->sm_count * 8 + groups - 1) / groups;
+  if (nchunks > 64) nchunks = 64;  // the finish pass merges nchunks partials per lane
+  const int64_t max_chunks = (a.R + 63) / 64;
+  if (nchunks > max_chunks) nchunks = max_chunks;
+  if (nchunks < 1) nchunks = 1;
+  a.chunk = (a.R + nchunks - 1) / nchunks;
+  nchunks = (a.R + a.chunk - 1) / a.chunk;
+  const int64_t grid = groups * nchunks;
+  if (grid > INT32_MAX) return fail(ACD_ERR_UNSUPPORTED, "softmax: grid too large");
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, sizeof(double2) * (size_t)grid * 256 * VL, s, &scratch));
+  double2 *part = static_cast<double2 *>(scratch);
+  k_softmax_wide_partials<T, VL><<<(int)grid, 256, 0, s>>>(a, nchunks, lblocks, part);
+  k_softmax_wide_finish<T, VL><<<(int)grid, 256, 0, s>>>(a, nchunks, lblocks, part);
+  return ACD_OK;
 }
 
 // ---- whole tensor ----------------------------------------------------------
@@ -178,9 +414,32 @@ static bool split_axis_sm(const acd_desc *in, const acd_desc *out, int axis, int
 }
 
 template <typename T, int LT>
+static acd_status launch_softmax_two_pass(acd_ctx *ctx, SoftArgs a, cudaStream_t s) {
+  a.lblocks = (a.L + LT - 1) / LT;
+  const int64_t groups = a.lblocks * a.O;
+  // chunks: enough CTAs to fill the GPU a few times, at least 256 steps each
+  int64_t nchunks = ((int64_t)ctx->sm_count * 8 + groups - 1) / groups;
+  const int64_t max_chunks = (a.R + 255) / 256;
+  if (nchunks > max_chunks) nchunks = max_chunks;
+  if (nchunks < 1) nchunks = 1;
+  a.chunk = (a.R + nchunks - 1) / nchunks;
+  nchunks = (a.R + a.chunk - 1) / a.chunk;
+  const int64_t grid = groups * nchunks;
+  if (grid > INT32_MAX) return fail(ACD_ERR_UNSUPPORTED, "softmax: grid too large");
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, sizeof(double2) * (size_t)grid * LT, s, &scratch));
+  double2 *part = static_cast<double2 *>(scratch);
+  k_softmax_partials<T, LT><<<(int)grid, 256, 0, s>>>(a, nchunks, part);
+  k_softmax_finish<T, LT><<<(int)grid, 256, 0, s>>>(a, nchunks, part);
+  return ACD_OK;
+}
+
+template <typename T, int LT>
 static acd_status launch_softmax_axis(acd_ctx *ctx, SoftArgs a, cudaStream_t s) {
   a.lblocks = (a.L + LT - 1) / LT;
   const int64_t groups = a.lblocks * a.O;
+  // chunks that would not fit shared memory even split over 8 CTAs: two passes
+  if (((a.R + 7) / 8) * (int64_t)LT * (int64_t)sizeof(T) > 160 * 1024) return launch_softmax_two_pass<T, LT>(ctx, a, s);
   // cluster size: enough CTAs to fill the GPU, chunks that fit shared memory
   const int64_t smem_target = 64 * 1024;
   const int64_t row_bytes = (int64_t)LT * sizeof(T);
@@ -270,7 +529,13 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
   a.orr = so[1];
   a.oo = so[2];
   acd_status st;
-  if (a.L == 1)
+  const int VL = f32 ? 4 : 2;
+  const bool wide = a.L >= 256 * VL && a.sl == 1 && a.ol == 1 && a.L % VL == 0 && a.sr % VL == 0 &&
+                    a.orr % VL == 0 && a.so % VL == 0 && a.oo % VL == 0 && aligned_to<char>(a.in, 16) &&
+                    aligned_to<char>(a.out, 16);
+  if (wide)
+    st = f32 ? launch_softmax_wide<float>(ctx, a, s) : launch_softmax_wide<double>(ctx, a, s);
+  else if (a.L == 1)
     st = f32 ? launch_softmax_axis<float, 1>(ctx, a, s) : launch_softmax_axis<double, 1>(ctx, a, s);
   else
     st = f32 ? launch_softmax_axis<float, 32>(ctx, a, s) : launch_softmax_axis<double, 16>(ctx, a, s);

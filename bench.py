@@ -42,6 +42,9 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=2)
     ap.add_argument("--n2", type=int, default=N2, help="extent of the sharded axis (default 32768)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--workload", default="views", choices=["views", "c1", "c2", "c3", "c4"],
+                    help="views (default, the sharded strided-views step) or a per-op report of one of the "
+                         "other configurations on one GPU")
     return ap.parse_args()
 
 
@@ -177,10 +180,148 @@ def cpu_baseline_single(sample_n2=256):
 
 
 # ---------------------------------------------------------------------------
+# per-op reports of the other configurations (one GPU)
+# ---------------------------------------------------------------------------
+def _time(fn, reps=10, warm=3):
+    import torch
+    for _ in range(warm):
+        fn()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / reps
+
+
+def _op(name, fn, nbytes, peak, reps=10, note=None):
+    ms = _time(fn, reps)
+    gbs = nbytes / (ms * 1e-3) / 1e9
+    d = {"op": name, "ms": round(ms, 4), "bytes": int(nbytes), "GB/s": round(gbs, 1), "frac": round(gbs / peak, 4)}
+    if note:
+        d["note"] = note
+    return d
+
+
+def run_config_report(a):
+    import numpy as np
+    import torch
+
+    import acediar as acd
+    import acediar.tensor as Tm
+
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    g = torch.Generator(device="cuda")
+    g.manual_seed(SEED)
+    ops = []
+    if a.workload == "c1":
+        n = 1 << 20
+        ta = acd.from_torch(torch.rand(n, generator=g, device="cuda", dtype=torch.float64), (n,), "double")
+        tb = acd.from_torch(torch.randn(n, generator=g, device="cuda", dtype=torch.float64), (n,), "double")
+        B = 8 * n
+        ops.append(_op("a+b", lambda: ta + tb, 3 * B, peak))
+        ops.append(_op("a*b", lambda: ta * tb, 3 * B, peak))
+        ops.append(_op("exp(a)", lambda: acd.exp(ta), 2 * B, peak))
+        ops.append(_op("sigmoid(b)", lambda: acd.sigmoid(tb), 2 * B, peak))
+        ops.append(_op("sqrt(a)", lambda: acd.sqrt(ta), 2 * B, peak))
+        c = ta + tb
+        ops.append(_op("sum(c)", lambda: acd.tensor_sum(c), B, peak))
+        ops.append(_op("var(c)", lambda: acd.tensor_var(c), B, peak))
+        ops.append(_op("which.max(c)", lambda: Tm._arg("argmax", c), B, peak))
+
+        def config():
+            c_ = ta + tb
+            d_ = ta * tb
+            e_ = acd.exp(ta)
+            f_ = acd.sigmoid(tb)
+            g_ = acd.sqrt(ta)
+            outs = []
+            for t in (c_, d_, e_, f_, g_):
+                outs += [acd.tensor_sum(t), acd.tensor_mean(t), acd.tensor_var(t)]
+            return outs
+        total_bytes = 3 * B * 2 + 2 * B * 3 + 15 * B + B
+        ops.append(_op("whole config (eager)", config, total_bytes, peak, note="20 launches, L2-resident 8 MiB arrays"))
+        # the same 20 launches captured once in a CUDA graph and replayed
+        for _ in range(3):
+            config()
+        torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
+        side = torch.cuda.Stream()
+        with torch.cuda.stream(side):
+            with torch.cuda.graph(graph, stream=side):
+                config()
+        torch.cuda.synchronize()
+        ops.append(_op("whole config (CUDA graph)", graph.replay, total_bytes, peak, reps=50,
+                       note="launch overhead removed; arrays stay in L2"))
+        workload = "elementwise chain + reductions, float64 n=2^20"
+        unit_elems = n
+    elif a.workload == "c2":
+        R = C = 8192
+        X = acd.from_torch(torch.randn(R * C, generator=g, device="cuda"), (R, C), "float")
+        r = acd.from_torch(torch.rand(C, generator=g, device="cuda") * 2 - 1, (1, C), "float")
+        B = 4 * R * C
+        Y = acd.fused("add_relu", X, r)
+        M = X > r
+        ops.append(_op("relu(X+r) fused", lambda: acd.fused("add_relu", X, r), 2 * B, peak))
+        ops.append(_op("X+r", lambda: X + r, 2 * B, peak))
+        ops.append(_op("X>r -> bool", lambda: X > r, B + R * C, peak))
+        ops.append(_op("pmax(X,r)", lambda: acd.pmax(X, r), 2 * B, peak))
+        ops.append(_op("tanh(X)*2 fused", lambda: acd.fused("tanh_scale", X, p0=2.0), 2 * B, peak))
+        ops.append(_op("colSums(Y)", lambda: acd.tensor_sum(Y, axis=[1]), B, peak))
+        ops.append(_op("count(M) per column", lambda: acd.tensor_count(M, axis=[1]), R * C, peak))
+        workload = "broadcast + compare, float32 8192x8192 + 1x8192"
+        unit_elems = R * C
+    elif a.workload == "c3":
+        shp = (4096, 4096, 16)
+        n = 4096 * 4096 * 16
+        T = acd.from_torch(torch.randn(n, generator=g, device="cuda"), shp, "float")
+        I = acd.from_torch(torch.randint(-1000, 1001, (n,), generator=g, device="cuda", dtype=torch.int32), shp, "int32")
+        B = 4 * n
+        for op in ("sum", "mean", "var", "max"):
+            ops.append(_op("%s(T)" % op, (lambda op=op: getattr(acd, "tensor_" + op)(T)), B, peak))
+        ops.append(_op("sum+var fused", lambda: acd.sum_var(T), B, peak, note="includes two 8-byte D2H reads"))
+        ops.append(_op("which.max(T)", lambda: Tm._arg("argmax", T), B, peak))
+        for ax in (1, 2, 3):
+            kept = n // shp[ax - 1]
+            for op in ("sum", "mean", "var", "max"):
+                ops.append(_op("%s(T, axis=%d)" % (op, ax), (lambda op=op, ax=ax: getattr(acd, "tensor_" + op)(T, axis=[ax])),
+                               B + 4 * kept, peak))
+            ops.append(_op("argmax(T, axis=%d)" % ax, (lambda ax=ax: acd.argmax(T, axis=ax)), B + 8 * kept, peak))
+        ops.append(_op("sum(int32 T)", lambda: acd.tensor_sum(I), B, peak))
+        U = acd.from_torch(torch.rand(64 * 1048576, generator=g, device="cuda"), (64, 1048576), "float")
+        ops.append(_op("cumsum(U, axis=2)", lambda: acd.cumsum(U, axis=2), 2 * 4 * 64 * 1048576, peak))
+        workload = "axis reductions float32 4096x4096x16, int32 sum, cumsum 64x1048576"
+        unit_elems = n
+    else:
+        R, C = 65536, 4096
+        Xf = acd.from_torch(torch.randn(R * C, generator=g, device="cuda") * 2.0, (R, C), "float")
+        off = acd.from_torch(torch.rand(R, generator=g, device="cuda") * 100 - 50, (R, 1), "float")
+        Xf = Xf + off
+        ops.append(_op("softmax f32 65536x4096 axis=2", lambda: acd.softmax(Xf, axis=2), 2 * 4 * R * C, peak))
+        R2, C2 = 1024, 32768
+        Xd = acd.from_torch(torch.randn(R2 * C2, generator=g, device="cuda", dtype=torch.float64), (R2, C2), "double")
+        ops.append(_op("softmax f64 1024x32768 axis=2", lambda: acd.softmax(Xd, axis=2), 2 * 8 * R2 * C2, peak))
+        ops.append(_op("softmax f32 whole tensor", lambda: acd.softmax(Xf), 3 * 4 * R * C, peak))
+        sm = acd.softmax(Xf, axis=2)
+        rows = acd.tensor_sum(sm, axis=[2]).as_array()
+        ops.append({"op": "row sums of f32 softmax", "max_abs_dev_from_1": float(np.abs(rows - 1).max())})
+        workload = "row softmax float32 65536x4096 (N(0,4) + row offset U(-50,50)), float64 1024x32768"
+        unit_elems = R * C
+    line = {"metric": "HBM GB/s per op (algorithmic bytes / CUDA-event time)", "workload": workload,
+            "peak_GB/s": peak, "peak_source": peak_kind, "ops": ops, "n_gpus": 1}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
 def main():
     a = parse()
     if a.impl == "reference":
         return reference_arm(a)
+    if a.workload != "views":
+        return run_config_report(a)
 
     import torch
     import torch.distributed as dist
@@ -286,6 +427,9 @@ def main():
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
     result_sum, result_var = float(tot.item()), float(var.item())
+    idx_host = idx.storage[:N0 * N1].cpu()
+    result_idx = {"checksum": int(idx_host.to(torch.int64).sum().item()), "first": int(idx_host[0].item()),
+                  "last": int(idx_host[-1].item())}
 
     # ---- per-kernel durations (CUDA events on the launching stream)
     kern = {}
@@ -366,7 +510,7 @@ def main():
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
-            "result": {"sum": result_sum, "var": result_var},
+            "result": {"sum": result_sum, "var": result_var, "argmax_axis1": result_idx},
         }
         print(json.dumps(line), flush=True)
     if world > 1:

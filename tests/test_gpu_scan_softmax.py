@@ -82,7 +82,7 @@ def test_scan_bounded_wait_reports_and_recovers(acd):
 @pytest.mark.parametrize("name", ["float", "double"])
 def test_softmax_along_axes(acd, name):
     rng = np.random.default_rng(5)
-    for shape in [(65, 4096), (1000, 33), (7, 3000), (33, 64, 5), (4, 40000), (2048, 8)]:
+    for shape in [(65, 4096), (1000, 33), (7, 3000), (33, 64, 5), (4, 40000), (2048, 8), (8192, 600), (1030, 70)]:
         x = (rng.normal(0, 2, shape) + rng.uniform(-50, 50, (shape[0],) + (1,) * (len(shape) - 1))).astype(NP[name])
         t = acd.as_tensor(x, dtype=name)
         for axis in range(1, len(shape) + 1):
