@@ -19,16 +19,233 @@
 //     at once) and publishes anyway, so the kernel always terminates.
 // Accumulation is float64 (a float64 sum per lane; R accumulates in long
 // double and rounds each output once).
+//
+// Interleaved lanes (L > 1: the scanned axis is not the innermost one, so
+// neighbouring lanes sit next to each other in memory) take a three-kernel
+// reduce-then-scan instead, which has no waits between CTAs:
+//   1. k_lane_reduce: one warp per (lane block, step segment) task reads its
+//      segment row by row (LT lanes x G step phases per warp, so a warp load
+//      covers G rows of LT lanes) and writes one total per lane;
+//   2. k_lane_seg_scan: one CTA per (chain, lane) turns the segment totals
+//      into exclusive prefixes in place;
+//   3. k_lane_apply: the same warps re-read their segments and write
+//      prefix + running sum.
+// The traffic is 3 tensor passes (read, read, write) against 2 for the
+// chained scan, but the chained scan's look-back frontier advances only one
+// 32-tile window per round trip, which caps it far below HBM speed when a
+// tile carries LT lane totals.
 #include "scan_kernel.cuh"
 
 namespace acd {
 
+struct LaneArgs {
+  const void *in;
+  void *out;
+  int64_t L, R, O;
+  int64_t sl, sr, so;  // input strides
+  int64_t ol, orr, oo; // output strides
+  int64_t lblocks;     // lane blocks of LT lanes
+  int64_t nchains;     // lblocks * O
+  int64_t SB;          // row blocks (G steps each) per segment
+  int64_t nseg;        // segments per chain
+  double *seg;         // [nchains][LT][nseg] totals, then exclusive prefixes
+};
+
+constexpr int kLaneU = 16;  // row blocks loaded per batch
+
+// Task t (segment-major, so consecutive warps read neighbouring lane blocks
+// of the same rows) -> chain, segment and this thread's lane.
+template <int LT>
+struct LaneTask {
+  int64_t s, chain, o, l, rs, re;
+  __device__ __forceinline__ LaneTask(const LaneArgs &a, int64_t t, int li) {
+    constexpr int G = 32 / LT;
+    s = t / a.nchains;
+    chain = t - s * a.nchains;
+    o = chain / a.lblocks;
+    l = (chain - o * a.lblocks) * LT + li;
+    rs = s * a.SB * G;
+    re = min(a.R, rs + a.SB * G);
+  }
+};
+
+template <typename T, bool PROD, int LT>
+__global__ void __launch_bounds__(256) k_lane_reduce(LaneArgs a) {
+  constexpr int G = 32 / LT, U = kLaneU;
+  const double ident = PROD ? 1.0 : 0.0;
+  const int wl = threadIdx.x & 31, li = wl % LT, g = wl / LT;
+  const int64_t ntask = a.nchains * a.nseg;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t step = (int64_t)G * a.sr;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < ntask; t += nw) {
+    const LaneTask<LT> k(a, t, li);
+    double acc = ident;
+    if (k.l < a.L && k.rs + g < k.re) {
+      int64_t n = (k.re - k.rs - g + G - 1) / G;
+      const T *p = static_cast<const T *>(a.in) + k.o * a.so + k.l * a.sl + (k.rs + g) * a.sr;
+      for (; n >= U; n -= U, p += U * step) {
+        T v[U];
+#pragma unroll
+        for (int j = 0; j < U; ++j) v[j] = p[j * step];
+#pragma unroll
+        for (int j = 0; j < U; ++j) acc = combine<PROD>(acc, (double)v[j]);
+      }
+      for (; n > 0; --n, p += step) acc = combine<PROD>(acc, (double)*p);
+    }
+#pragma unroll
+    for (int d = LT; d < 32; d <<= 1) acc = combine<PROD>(acc, __shfl_xor_sync(0xffffffffu, acc, d));
+    if (g == 0) a.seg[(k.chain * LT + li) * a.nseg + k.s] = acc;
+  }
+}
+
+// Exclusive scan, in place, of each of `nrows` rows of `nseg` (<= 4096)
+// segment totals: 256 threads x 16 consecutive items.
+template <bool PROD>
+__global__ void __launch_bounds__(256) k_lane_seg_scan(double *seg, int64_t nrows, int nseg) {
+  constexpr int IPT = 16;
+  __shared__ double s_warp[8];
+  const double ident = PROD ? 1.0 : 0.0;
+  const int wl = threadIdx.x & 31, w = threadIdx.x >> 5;
+  const int i0 = threadIdx.x * IPT;
+  for (int64_t row = blockIdx.x; row < nrows; row += gridDim.x) {
+    double *p = seg + row * nseg;
+    double v[IPT];
+    double tot = ident;
+#pragma unroll
+    for (int j = 0; j < IPT; ++j) {
+      v[j] = (i0 + j < nseg) ? p[i0 + j] : ident;
+      tot = combine<PROD>(tot, v[j]);
+    }
+    double x = tot;
+#pragma unroll
+    for (int d = 1; d < 32; d <<= 1) {
+      const double y = __shfl_up_sync(0xffffffffu, x, d);
+      if (wl >= d) x = combine<PROD>(y, x);
+    }
+    if (wl == 31) s_warp[w] = x;
+    __syncthreads();
+    double run = ident;
+    for (int k = 0; k < w; ++k) run = combine<PROD>(run, s_warp[k]);
+    double prev = __shfl_up_sync(0xffffffffu, x, 1);
+    if (wl > 0) run = combine<PROD>(run, prev);
+#pragma unroll
+    for (int j = 0; j < IPT; ++j) {
+      if (i0 + j < nseg) p[i0 + j] = run;
+      run = combine<PROD>(run, v[j]);
+    }
+    __syncthreads();
+  }
+}
+
+template <typename T, bool PROD, int LT>
+__global__ void __launch_bounds__(256) k_lane_apply(LaneArgs a) {
+  constexpr int G = 32 / LT, U = kLaneU;
+  const double ident = PROD ? 1.0 : 0.0;
+  const int wl = threadIdx.x & 31, li = wl % LT, g = wl / LT;
+  const int64_t ntask = a.nchains * a.nseg;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  const int64_t step = (int64_t)G * a.sr, ostep = (int64_t)G * a.orr;
+  for (int64_t t = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5; t < ntask; t += nw) {
+    const LaneTask<LT> k(a, t, li);
+    const bool lok = k.l < a.L;
+    const int64_t lc = lok ? k.l : 0;  // lanes past L read lane 0 and discard it
+    double carry = a.nseg > 1 ? a.seg[(k.chain * LT + li) * a.nseg + k.s] : ident;
+    const T *p = static_cast<const T *>(a.in) + k.o * a.so + lc * a.sl + (k.rs + g) * a.sr;
+    T *q = static_cast<T *>(a.out) + k.o * a.oo + lc * a.ol + (k.rs + g) * a.orr;
+    const int64_t nfull = (k.re - k.rs) / G;          // row blocks with all G steps present
+    const int64_t nb = (k.re - k.rs + G - 1) / G;     // all row blocks
+    int64_t b = 0;
+    for (; b + U <= nfull; b += U, p += U * step, q += U * ostep) {
+      T v[U];
+#pragma unroll
+      for (int j = 0; j < U; ++j) v[j] = p[j * step];
+#pragma unroll
+      for (int j = 0; j < U; ++j) {
+        double x = lok ? (double)v[j] : ident;
+#pragma unroll
+        for (int d = 1; d < G; d <<= 1) {
+          const double y = __shfl_up_sync(0xffffffffu, x, d * LT);
+          if (g >= d) x = combine<PROD>(y, x);
+        }
+        if (lok) q[j * ostep] = (T)combine<PROD>(carry, x);
+        if constexpr (G == 1)
+          carry = combine<PROD>(carry, x);
+        else
+          carry = combine<PROD>(carry, __shfl_sync(0xffffffffu, x, (G - 1) * LT + li));
+      }
+    }
+    for (; b < nb; ++b, p += step, q += ostep) {
+      const bool ok = lok && k.rs + b * G + g < k.re;
+      double x = ok ? (double)*p : ident;
+#pragma unroll
+      for (int d = 1; d < G; d <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, x, d * LT);
+        if (g >= d) x = combine<PROD>(y, x);
+      }
+      if (ok) *q = (T)combine<PROD>(carry, x);
+      carry = combine<PROD>(carry, __shfl_sync(0xffffffffu, x, (G - 1) * LT + li));
+    }
+  }
+}
+
+template <typename T, bool PROD, int LT>
+static acd_status launch_lane_scan_lt(acd_ctx *ctx, LaneArgs a, cudaStream_t s) {
+  constexpr int G = 32 / LT, U = kLaneU;
+  a.lblocks = (a.L + LT - 1) / LT;
+  a.nchains = a.lblocks * a.O;
+  const int64_t RB = (a.R + G - 1) / G;
+  // about one task per resident warp, at most 4096 segments per chain and
+  // at least U row blocks per segment
+  const int64_t target = (int64_t)ctx->sm_count * 64;
+  int64_t nseg = (target + a.nchains - 1) / a.nchains;
+  if (nseg > 4096) nseg = 4096;
+  if (nseg < 1) nseg = 1;
+  int64_t SB = (RB + nseg - 1) / nseg;
+  if (SB < U) SB = U;
+  SB = (SB + U - 1) / U * U;
+  a.SB = SB;
+  a.nseg = (RB + SB - 1) / SB;
+  const int64_t ntask = a.nchains * a.nseg;
+  if (a.nseg > 1) {
+    void *scratch;
+    ACD_TRY(get_scratch(ctx, (size_t)(a.nchains * LT * a.nseg) * sizeof(double), s, &scratch));
+    a.seg = static_cast<double *>(scratch);
+    k_lane_reduce<T, PROD, LT>
+        <<<persistent_grid(ctx, k_lane_reduce<T, PROD, LT>, 256, 0, (ntask + 7) / 8), 256, 0, s>>>(a);
+    const int64_t nrows = a.nchains * LT;
+    const int sg = (int)(nrows < (int64_t)ctx->sm_count * 8 ? nrows : (int64_t)ctx->sm_count * 8);
+    k_lane_seg_scan<PROD><<<sg, 256, 0, s>>>(a.seg, nrows, (int)a.nseg);
+  }
+  k_lane_apply<T, PROD, LT><<<persistent_grid(ctx, k_lane_apply<T, PROD, LT>, 256, 0, (ntask + 7) / 8), 256, 0, s>>>(a);
+  return ACD_OK;
+}
+
+template <typename T, bool PROD>
+static acd_status launch_lane_scan(acd_ctx *ctx, const ScanArgs &sa, cudaStream_t s) {
+  LaneArgs a{};
+  a.in = sa.in;
+  a.out = sa.out;
+  a.L = sa.L;
+  a.R = sa.R;
+  a.O = sa.O;
+  a.sl = sa.sl;
+  a.sr = sa.sr;
+  a.so = sa.so;
+  a.ol = sa.ol;
+  a.orr = sa.orr;
+  a.oo = sa.oo;
+  if (a.L > 16) return launch_lane_scan_lt<T, PROD, 32>(ctx, a, s);
+  if (a.L > 8) return launch_lane_scan_lt<T, PROD, 16>(ctx, a, s);
+  if (a.L > 4) return launch_lane_scan_lt<T, PROD, 8>(ctx, a, s);
+  if (a.L > 2) return launch_lane_scan_lt<T, PROD, 4>(ctx, a, s);
+  return launch_lane_scan_lt<T, PROD, 2>(ctx, a, s);
+}
+
 template <typename T, bool PROD>
 static acd_status launch_scan(acd_ctx *ctx, ScanArgs a, cudaStream_t s) {
-  constexpr int LTW = 128 / sizeof(T);  // lanes per tile when L > 1: 128-byte rows
-  const int LT = a.L == 1 ? 1 : LTW;
-  constexpr int SEG1 = 16, SEGW = 32;
-  const int RT = LT == 1 ? 256 * SEG1 : (256 / LTW) * SEGW;
+  if (a.L > 1) return launch_lane_scan<T, PROD>(ctx, a, s);
+  constexpr int LT = 1, SEG1 = 16;
+  const int RT = 256 * SEG1;
   a.lblocks = (a.L + LT - 1) / LT;
   a.rtiles = (a.R + RT - 1) / RT;
   a.ntiles = a.lblocks * a.O * a.rtiles;
@@ -47,10 +264,7 @@ static acd_status launch_scan(acd_ctx *ctx, ScanArgs a, cudaStream_t s) {
   a.epoch = ctx->epoch;
   a.fault_tile = ctx->scan_fault_tile;
   a.timeout_ns = ctx->scan_timeout_ns;
-  if (LT == 1)
-    k_scan<T, PROD, 1, SEG1><<<(int)a.ntiles, 256, 0, s>>>(a);
-  else
-    k_scan<T, PROD, LTW, SEGW><<<(int)a.ntiles, 256, 0, s>>>(a);
+  k_scan<T, PROD, 1, SEG1><<<(int)a.ntiles, 256, 0, s>>>(a);
   return ACD_OK;
 }
 

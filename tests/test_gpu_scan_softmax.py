@@ -47,6 +47,18 @@ def test_cumsum_along_axes(acd, name):
 
 
 @pytest.mark.parametrize("name", ["float", "double"])
+def test_cumprod_along_axes(acd, name):
+    """Interleaved lanes of every lane-block width (1..33 lanes), one and many
+    segments per chain, and an outer axis."""
+    rng = np.random.default_rng(5)
+    for shape, axis in [((2, 40000), 2), ((5, 20000), 2), ((12, 7000), 2), ((33, 3000), 2), ((40, 17, 30), 2),
+                        ((3, 4, 9000), 3), ((16, 700), 2)]:
+        x = rng.uniform(0.999, 1.001, shape).astype(NP[name])
+        got = acd.cumprod(acd.as_tensor(x, dtype=name), axis=axis).as_array()
+        assert_rel(got, oracle.scan("cumprod", x, axis - 1), TOL[name] * 10, "cumprod %s axis %d" % (shape, axis))
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
 def test_cumsum_of_view(acd, name):
     rng = np.random.default_rng(4)
     x = rng.uniform(0, 1, (50, 70)).astype(NP[name])
