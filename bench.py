@@ -31,6 +31,10 @@ CHUNK = 128  # slices along axis 3 generated per seed (independent of the GPU co
 SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
 BYTES_PER_ELEM = {"transpose": 8, "fused_chain": 8, "stats": 4, "argmax_keys": 4}
+# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 13
+# launches) on the 256x512x1024 case of the same step, scaled by elements to a full launch.  Reads are
+# exactly 4 B/elem; the write side reads low by the ~48 MB of dirty lines still in L2 when a launch ends.
+TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.638, "fused_chain": 7.639, "stats": 4.001, "argmax_keys": 4.008}
 
 
 def parse():
@@ -451,7 +455,7 @@ def main():
         byts = BYTES_PER_ELEM[name] * nloc
         gbs = byts / (kms * 1e-3) / 1e9
         ops.append({"kernel": name, "ms": round(kms, 4), "bytes": byts, "GB/s": round(gbs, 1),
-                    "frac": round(gbs / peak, 4)})
+                    "frac": round(gbs / peak, 4), "traffic": int(TRAFFIC_BYTES_PER_ELEM[name] * nloc)})
     top = max(ops, key=lambda o: o["ms"])
 
     # ---- end to end: host buffers in, results out, through the same C ABI
@@ -503,8 +507,9 @@ def main():
                        "parallelism": "shard%d" % world, "elements": ntot},
             "algorithmic_GB/s": round(24 * ntot / (ms_max * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": top["GB/s"], "peak": peak, "unit": "GB/s",
-                         "frac": round(top["GB/s"] / peak, 4), "traffic": None, "kernel": top["kernel"],
-                         "peak_source": peak_kind},
+                         "frac": round(top["GB/s"] / peak, 4), "traffic": top["traffic"], "kernel": top["kernel"],
+                         "peak_source": peak_kind, "traffic_source": "ncu dram bytes/elem of the 256x512x1024 "
+                         "case x elements per launch"},
             "ops": ops,
             "gpu_launches": LAUNCHES_PER_STEP * a.steps,
             "clocks": clk,
