@@ -19,6 +19,7 @@
 //   k_general   anything else: int64 coordinates, incremented along a run.
 #include "common.cuh"
 #include "ops.cuh"
+#include "tma.cuh"
 
 namespace acd {
 
@@ -361,6 +362,9 @@ template <typename T, int TILE>
 static void launch_transpose(acd_ctx *ctx, T *out, const T *in, int64_t n0, int64_t n1, int64_t n2, int64_t os1,
                              int64_t os2, int64_t is0, int64_t is2, cudaStream_t stream) {
   constexpr int V = (sizeof(T) >= 4) ? 16 / (int)sizeof(T) : 1;
+  if constexpr (sizeof(T) == 4) {
+    if (launch_transpose_tma4(ctx, out, in, n0, n1, n2, os1, os2, is0, is2, stream)) return;
+  }
   const int64_t tiles0 = (n0 + TILE - 1) / TILE, tiles1 = (n1 + TILE - 1) / TILE;
   const int64_t ntiles = tiles0 * tiles1 * n2;
   static bool carveout_set = false;  // one shared-memory carveout request per instantiation

@@ -1,0 +1,101 @@
+// Tensor Memory Accelerator (TMA) and mbarrier helpers for sm_100a, as
+// inline PTX, plus the host-side tensor-map encoder.
+//
+// Only plain tiled loads and stores are used: no cluster multicast (every
+// load names this CTA's own shared memory and an mbarrier in it).
+#pragma once
+
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+
+namespace acd {
+
+__device__ __forceinline__ uint32_t smem_addr(const void *p) { return (uint32_t)__cvta_generic_to_shared(p); }
+
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_addr(bar)), "r"(count) : "memory");
+}
+
+// Makes mbarrier initialisation visible to the async proxy (TMA).
+__device__ __forceinline__ void mbar_init_fence() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+// One arrival that also expects `bytes` of TMA transactions in this phase.
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n selp.u32 %0, 1, 0, p;\n}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for the phase with `parity` to complete, at most `timeout_ns`.
+// Returns false when the limit expired.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const uint64_t t0 = global_timer_ns();
+  while (!mbar_try_wait(bar, parity))
+    if (global_timer_ns() - t0 > timeout_ns) return false;
+  return true;
+}
+
+// 3-D tiled load of one box into shared memory; completion is counted on `bar`.
+__device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, uint64_t *bar, int c0, int c1,
+                                            int c2) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_addr(dst)),
+      "l"(map), "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(bar))
+      : "memory");
+}
+
+// 3-D tiled store of one box from shared memory (bulk-group completion).
+// Parts of the box outside the tensor are not written.
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap *map, const void *src, int c0, int c1, int c2) {
+  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(map),
+               "r"(c0), "r"(c1), "r"(c2), "r"(smem_addr(src))
+               : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+// Waits until at most N committed store groups still read shared memory.
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+  asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+// Orders this thread's generic-proxy shared-memory writes before later
+// async-proxy (TMA) reads of them.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Host: encodes a 3-D tiled tensor map over 4- or 8-byte elements with a
+// 128-byte swizzle (box inner extent = 128 bytes).  dims[0] is the contiguous
+// axis; strides_elems[0..1] are the element strides of dims 1 and 2.
+// Returns false when the driver rejects the map (alignment, extents).
+bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, const int64_t dims[3],
+                          const int64_t strides_elems[2], const uint32_t box[3]);
+
+// Host: TMA-staged transpose of 4-byte elements, out(i,j,k) = in(i,j,k) with
+// out contiguous along i (extent n0, j stride os1, k stride os2) and in
+// contiguous along j (extent n1, i stride is0, k stride is2).  Returns false,
+// having launched nothing, when the views do not meet TMA's alignment rules
+// or are too small to gain from it.
+bool launch_transpose_tma4(acd_ctx *ctx, void *out, const void *in, int64_t n0, int64_t n1, int64_t n2,
+                           int64_t os1, int64_t os2, int64_t is0, int64_t is2, cudaStream_t stream);
+
+}  // namespace acd

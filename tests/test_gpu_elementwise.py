@@ -163,6 +163,24 @@ def test_fused_chains_bit_identical(acd, dt, name):
     assert_exact(acd.fused("tanh_scale", t, p0=2.0).as_array(), (acd.tanh(t) * 2.0).as_array(), "tanh_scale")
 
 
+@pytest.mark.parametrize("name,dt", [("float", np.float32), ("int32", np.int32)])
+def test_copy_transpose_tma_shapes(acd, name, dt):
+    """4-byte transposes whose strides suit the TMA path: full and ragged
+    64x64 tiles, a batch axis, the strided-views permutation at reduced size,
+    and extents just past a tile edge (boxes wholly outside the tensor)."""
+    rng = np.random.default_rng(11)
+    cases = [((64, 64), (2, 1)), ((256, 132), (2, 1)), ((1000, 2052), (2, 1)), ((68, 100, 3), (2, 1, 3)),
+             ((64, 72, 5), (2, 1, 3)), ((72, 5, 64), (3, 2, 1)), ((256, 512, 64), (3, 1, 2)),
+             ((96, 4, 260), (3, 2, 1)), ((100, 68), (2, 1)), ((260, 68), (2, 1))]
+    for shape, perm in cases:
+        x = (rng.normal(size=shape) * 1000).astype(dt)
+        t = acd.as_tensor(x, dtype=name)
+        got = acd.contiguous(acd.permute_view(t, list(perm))).as_array()
+        assert_exact(got, np.transpose(x, [p - 1 for p in perm]), "%s perm %s" % (shape, perm))
+    # status word clean: no pipeline wait expired
+    acd.check_device_status()
+
+
 @pytest.mark.parametrize("name,dt", [("float", np.float32), ("double", np.float64), ("int32", np.int32),
                                      ("int64", np.int64), ("bool", np.bool_)])
 def test_copy_permutations_bit_exact(acd, name, dt):
