@@ -35,6 +35,7 @@ __device__ __forceinline__ typename F::Out apply(const F &f, typename F::In a, t
 // kernels
 // ---------------------------------------------------------------------------
 constexpr int kEwThreads = 256;
+constexpr int kFlatU = 4;  // 16-byte vectors in flight per thread and operand
 
 template <class F, int V, int U>
 __global__ void __launch_bounds__(kEwThreads) k_flat(typename F::Out *__restrict__ out,
@@ -55,26 +56,32 @@ __global__ void __launch_bounds__(kEwThreads) k_flat(typename F::Out *__restrict
   const Vec<T, V> *av = reinterpret_cast<const Vec<T, V> *>(a + head);
   const Vec<T, V> *bv = reinterpret_cast<const Vec<T, V> *>(F::kIn == 2 ? b + head : a + head);
   Vec<O, V> *ov = reinterpret_cast<Vec<O, V> *>(out + head);
-  for (int64_t v0 = tid; v0 < nvec; v0 += nth * U) {
+  // full groups of U vectors: every load is in range, so none is guarded and
+  // all U are in flight before the first use
+  int64_t v0 = tid;
+  for (; v0 + (int64_t)(U - 1) * nth < nvec; v0 += nth * U) {
     Vec<T, V> xa[U], xb[U];
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t v = v0 + (int64_t)u * nth;
-      if (v < nvec) {
-        xa[u] = av[v];
-        if constexpr (F::kIn == 2) xb[u] = bv[v];
-      }
+      xa[u] = av[v0 + (int64_t)u * nth];
+      if constexpr (F::kIn == 2) xb[u] = bv[v0 + (int64_t)u * nth];
     }
 #pragma unroll
     for (int u = 0; u < U; ++u) {
-      const int64_t v = v0 + (int64_t)u * nth;
-      if (v < nvec) {
-        Vec<O, V> r;
+      Vec<O, V> r;
 #pragma unroll
-        for (int k = 0; k < V; ++k) r.v[k] = apply(f, xa[u].v[k], F::kIn == 2 ? xb[u].v[k] : T(0));
-        ov[v] = r;
-      }
+      for (int k = 0; k < V; ++k) r.v[k] = apply(f, xa[u].v[k], F::kIn == 2 ? xb[u].v[k] : T(0));
+      ov[v0 + (int64_t)u * nth] = r;
     }
+  }
+  for (; v0 < nvec; v0 += nth) {
+    const Vec<T, V> xa = av[v0];
+    Vec<T, V> xb;
+    if constexpr (F::kIn == 2) xb = bv[v0];
+    Vec<O, V> r;
+#pragma unroll
+    for (int k = 0; k < V; ++k) r.v[k] = apply(f, xa.v[k], F::kIn == 2 ? xb.v[k] : T(0));
+    ov[v0] = r;
   }
 }
 
@@ -313,9 +320,9 @@ static acd_status launch_map(acd_ctx *ctx, const F &f, const acd_desc *out, cons
     const bool ok = aligned_to<T>(pa, sizeof(T)) && aligned_to<O>(po, sizeof(O)) && ca == co && cb == ca;
     const int64_t head = ok ? (V - ca) % V : n;
     const int64_t head_c = head > n ? n : head;
-    const int64_t work = ((ok ? (n - head_c) / V + 1 : n) + kEwThreads * 2 - 1) / (kEwThreads * 2);
-    const int grid = persistent_grid(ctx, k_flat<F, V, 2>, kEwThreads, 0, work);
-    k_flat<F, V, 2><<<grid, kEwThreads, 0, stream>>>(po, pa, pb, n, head_c, f);
+    const int64_t work = ((ok ? (n - head_c) / V + 1 : n) + kEwThreads * kFlatU - 1) / (kEwThreads * kFlatU);
+    const int grid = persistent_grid(ctx, k_flat<F, V, kFlatU>, kEwThreads, 0, work);
+    k_flat<F, V, kFlatU><<<grid, kEwThreads, 0, stream>>>(po, pa, pb, n, head_c, f);
     return ACD_OK;
   }
 

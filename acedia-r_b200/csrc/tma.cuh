@@ -83,12 +83,15 @@ __device__ __forceinline__ void fence_proxy_async_smem() {
   asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
-// Host: encodes a 3-D tiled tensor map over 4- or 8-byte elements with a
-// 128-byte swizzle (box inner extent = 128 bytes).  dims[0] is the contiguous
-// axis; strides_elems[0..1] are the element strides of dims 1 and 2.
-// Returns false when the driver rejects the map (alignment, extents).
+// Host: encodes a 3-D tiled tensor map over 4- or 8-byte elements, with a
+// 128-byte swizzle (box inner extent = 128 bytes) or none.  dims[0] is the
+// contiguous axis; strides_elems[0..1] are the element strides of dims 1 and
+// 2.  `promote256` lets L2 fetch 256-byte granules (worth it when the
+// neighbouring 128 bytes are read at about the same time).  Returns false
+// when the driver rejects the map (alignment, extents).
 bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, const int64_t dims[3],
-                          const int64_t strides_elems[2], const uint32_t box[3]);
+                          const int64_t strides_elems[2], const uint32_t box[3], bool swizzle128 = true,
+                          bool promote256 = true);
 
 // Host: TMA-staged transpose of 4-byte elements, out(i,j,k) = in(i,j,k) with
 // out contiguous along i (extent n0, j stride os1, k stride os2) and in

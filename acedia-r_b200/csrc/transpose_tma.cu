@@ -211,7 +211,8 @@ PFN_cuTensorMapEncodeTiled_v12000 tensor_map_encoder() {
 }  // namespace
 
 bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, const int64_t dims[3],
-                          const int64_t strides_elems[2], const uint32_t box[3]) {
+                          const int64_t strides_elems[2], const uint32_t box[3], bool swizzle128,
+                          bool promote256) {
   auto enc = tensor_map_encoder();
   if (!enc) return false;
   cuuint64_t gd[3], gs[2];
@@ -221,7 +222,8 @@ bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, co
   cuuint32_t es[3] = {1, 1, 1};
   const CUtensorMapDataType dt = elem_bytes == 8 ? CU_TENSOR_MAP_DATA_TYPE_UINT64 : CU_TENSOR_MAP_DATA_TYPE_UINT32;
   return enc(map, dt, 3, const_cast<void *>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-             CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+             swizzle128 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_NONE,
+             promote256 ? CU_TENSOR_MAP_L2_PROMOTION_L2_256B : CU_TENSOR_MAP_L2_PROMOTION_NONE,
              CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 

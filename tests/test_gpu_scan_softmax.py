@@ -104,6 +104,26 @@ def test_softmax_along_axes(acd, name):
 
 
 @pytest.mark.parametrize("name", ["float", "double"])
+def test_softmax_rows_contiguous_lanes(acd, name):
+    """Row softmax of column-major matrices (lanes contiguous): the two-pass
+    wide kernels (4096+ lanes) and the single-read cluster kernel (fewer
+    lanes: whole rows in a cluster's shared memory), with ragged lane blocks,
+    steps past the last box, an outer axis, -inf entries and a row offset of
+    +-50."""
+    rng = np.random.default_rng(7)
+    for shape, axis in [((4096, 2048), 2), ((2048, 700), 2), ((4100, 1200), 2), ((4096, 500, 2), 2),
+                        ((8192, 96), 2), ((6000, 5000), 2), ((960, 4000), 2), ((500, 2500), 2),
+                        ((600, 700, 3), 2), ((1000, 300), 2)]:
+        x = (rng.normal(0, 2, shape) + rng.uniform(-50, 50, (shape[0],) + (1,) * (len(shape) - 1))).astype(NP[name])
+        x.reshape(-1)[::977] = -np.inf
+        t = acd.as_tensor(x, dtype=name)
+        got = acd.softmax(t, axis=axis).as_array()
+        exp = oracle.softmax(x, axis - 1)
+        assert_rel(got, exp, TOL[name], "softmax %s axis %d" % (shape, axis), atol=ATOL[name])
+    acd.check_device_status()
+
+
+@pytest.mark.parametrize("name", ["float", "double"])
 def test_softmax_whole_tensor(acd, name):
     rng = np.random.default_rng(6)
     for n in [1, 5, 1000, (1 << 20) + 1]:
