@@ -106,18 +106,12 @@ __global__ void __launch_bounds__(kRedThreads) k_red_flat(const T *__restrict__ 
 #pragma unroll
     for (int u = 0; u < U; ++u) x[u] = pv[v0 + (int64_t)u * nth];
 #pragma unroll
-    for (int u = 0; u < U; ++u) {
-      const int64_t v = v0 + (int64_t)u * nth;
-#pragma unroll
-      for (int k = 0; k < V; ++k) part[u].add(x[u].v[k], head + v * V + k);
-    }
+    for (int u = 0; u < U; ++u) acc_add_vec(part[u], x[u], head + (v0 + (int64_t)u * nth) * V);
   }
   // remainder: fewer than U vectors left for this thread
   for (int u = 0; v0 + (int64_t)u * nth < nvec; ++u) {
     const int64_t v = v0 + (int64_t)u * nth;
-    const Vec<T, V> x = pv[v];
-#pragma unroll
-    for (int k = 0; k < V; ++k) part[0].add(x.v[k], head + v * V + k);
+    acc_add_vec(part[0], pv[v], head + v * V);
   }
 #pragma unroll
   for (int u = 0; u < U; ++u) acc.merge(part[u]);
@@ -185,21 +179,20 @@ __global__ void __launch_bounds__(256) k_red_inner_warp(const T *__restrict__ in
     acc.init();
     if constexpr (Acc::kShift) acc.set_shift(p[0]);
     if constexpr (VEC) {
-      constexpr int U = 4;
+      // bytes (bool counts) carry 16 elements per vector and little state per
+      // element: keep 8 vectors in flight per lane
+      constexpr int U = sizeof(T) == 1 ? 8 : 4;
       const int64_t nv = R / V;
       const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(p);
-      for (int64_t v0 = lane; v0 < nv; v0 += 32 * U) {
+      int64_t v0 = lane;
+      for (; v0 + 32 * (U - 1) < nv; v0 += 32 * U) {  // U full vectors: unguarded loads
         Vec<T, V> x[U];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (v0 + 32 * u < nv) x[u] = pv[v0 + 32 * u];
+        for (int u = 0; u < U; ++u) x[u] = pv[v0 + 32 * u];
 #pragma unroll
-        for (int u = 0; u < U; ++u)
-          if (v0 + 32 * u < nv) {
-#pragma unroll
-            for (int k = 0; k < V; ++k) acc.add(x[u].v[k], (v0 + 32 * u) * V + k);
-          }
+        for (int u = 0; u < U; ++u) acc_add_vec(acc, x[u], (v0 + 32 * u) * V);
       }
+      for (; v0 < nv; v0 += 32) acc_add_vec(acc, pv[v0], v0 * V);
       for (int64_t r = nv * V + lane; r < R; r += 32) acc.add(p[r], r);
     } else {
       for (int64_t r = lane; r < R; r += 32) acc.add(p[r * sr], r);
@@ -232,20 +225,15 @@ __global__ void __launch_bounds__(kRedThreads) k_red_inner_cta(const T *__restri
     const int64_t v_beg = r0 / V, v_end = r1 / V;
     const Vec<T, V> *pv = reinterpret_cast<const Vec<T, V> *>(p);
     constexpr int U = 4;
-    for (int64_t v0 = v_beg + threadIdx.x; v0 < v_end; v0 += (int64_t)blockDim.x * U) {
+    int64_t v0 = v_beg + threadIdx.x;
+    for (; v0 + (int64_t)blockDim.x * (U - 1) < v_end; v0 += (int64_t)blockDim.x * U) {  // unguarded
       Vec<T, V> x[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u)
-        if (v0 + (int64_t)blockDim.x * u < v_end) x[u] = pv[v0 + (int64_t)blockDim.x * u];
+      for (int u = 0; u < U; ++u) x[u] = pv[v0 + (int64_t)blockDim.x * u];
 #pragma unroll
-      for (int u = 0; u < U; ++u) {
-        const int64_t v = v0 + (int64_t)blockDim.x * u;
-        if (v < v_end) {
-#pragma unroll
-          for (int k = 0; k < V; ++k) acc.add(x[u].v[k], v * V + k);
-        }
-      }
+      for (int u = 0; u < U; ++u) acc_add_vec(acc, x[u], (v0 + (int64_t)blockDim.x * u) * V);
     }
+    for (; v0 < v_end; v0 += blockDim.x) acc_add_vec(acc, pv[v0], v0 * V);
     for (int64_t r = v_end * V + threadIdx.x; r < r1; r += blockDim.x) acc.add(p[r], r);
   } else {
     for (int64_t r = r0 + threadIdx.x; r < r1; r += blockDim.x) acc.add(p[r * sr], r);

@@ -139,6 +139,30 @@ struct CountAcc {
   __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const { store_i(os.out, os.dt, oi, c); }
 };
 
+// Nonzero bytes of a 32-bit word: each byte's bits are folded into its bit 0
+// (the shifts stay inside the byte for bits 0..3, which are all that is
+// kept), then the marks are counted.
+__device__ __forceinline__ int nonzero_bytes(uint32_t w) {
+  uint32_t t = w | (w >> 4);
+  t |= t >> 2;
+  t |= t >> 1;
+  return __popc(t & 0x01010101u);
+}
+
+// Adds one vector of V elements to a single accumulator: a count over bytes
+// (bool) takes 4 bytes per instruction, everything else element by element
+// (`first` is the index of element 0, used by the argmin/argmax rules).
+template <class Acc, typename T, int V>
+__device__ __forceinline__ void acc_add_vec(Acc &acc, const Vec<T, V> &x, int64_t first) {
+  if constexpr (std::is_same<Acc, CountAcc<uint8_t>>::value && V == 16) {
+    const uint4 w = *reinterpret_cast<const uint4 *>(&x);
+    acc.c += nonzero_bytes(w.x) + nonzero_bytes(w.y) + nonzero_bytes(w.z) + nonzero_bytes(w.w);
+  } else {
+#pragma unroll
+    for (int k = 0; k < V; ++k) acc.add(x.v[k], first + k);
+  }
+}
+
 template <typename T, bool MAX>
 struct ExtAcc {
   static constexpr bool kShift = false;
