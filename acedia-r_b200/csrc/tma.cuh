@@ -1,8 +1,9 @@
 // Tensor Memory Accelerator (TMA) and mbarrier helpers for sm_100a, as
 // inline PTX, plus the host-side tensor-map encoder.
 //
-// Only plain tiled loads and stores are used: no cluster multicast (every
-// load names this CTA's own shared memory and an mbarrier in it).
+// Only plain tiled loads and stores of this GPU's own memory are used: every
+// load names this CTA's own shared memory and an mbarrier in it, and no load
+// is broadcast to other CTAs.
 #pragma once
 
 #include <cuda.h>

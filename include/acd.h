@@ -128,7 +128,9 @@ acd_status acd_ctx_destroy(acd_ctx *ctx);
  * Frees the current workspace; safe only when no call on `ctx` is in flight. */
 acd_status acd_ctx_set_allocator(acd_ctx *ctx, acd_alloc_fn alloc, acd_free_fn free_fn, void *user);
 /* Reads and clears the device status word (synchronises `stream`).
- * Returns ACD_ERR_DEVICE and fills *code when a kernel reported an error. */
+ * Returns ACD_ERR_DEVICE and fills *code when a kernel reported an error:
+ * 1 = the scan's look-back wait expired, 2 = a wait of the TMA transpose
+ * pipeline expired, 3 = the TMA load wait of the cluster softmax expired. */
 acd_status acd_ctx_check(acd_ctx *ctx, acd_stream stream, int32_t *code);
 /* Test hook for the bounded look-back wait of the scan: when `tile` >= 0,
  * the scan kernel's tile with that index never publishes its prefix, so the
