@@ -262,8 +262,14 @@ __global__ void __launch_bounds__(kRedThreads) k_red_inner_cta(const T *__restri
 
 // ---- outer axis: out[i + I*o] = reduce_r in[i*si + r*sr + o*so] -----------
 // A CTA covers TI = 32*V*WI consecutive i; WR warps split the r range.
+// Accumulators of more than 16 bytes (variance: shift and two float64 sums)
+// x 4 lanes would take ~100 registers and leave 2 CTAs per SM, too few loads
+// in flight; they are held to 3 CTAs per SM.
+template <class Acc>
+constexpr int outer_min_blocks() { return sizeof(Acc) > 16 ? 3 : 1; }
+
 template <class Acc, typename T, int V, int WR, bool VEC>
-__global__ void __launch_bounds__(256) k_red_outer(const T *__restrict__ in, int64_t I, int64_t R, int64_t si,
+__global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(const T *__restrict__ in, int64_t I, int64_t R, int64_t si,
                                                    int64_t sr, int64_t so, int64_t O, int64_t S, int64_t chunk,
                                                    int64_t itiles, Acc *__restrict__ partials,
                                                    unsigned int *counters, OutSpec os) {

@@ -58,6 +58,20 @@ def test_cumprod_along_axes(acd, name):
         assert_rel(got, oracle.scan("cumprod", x, axis - 1), TOL[name] * 10, "cumprod %s axis %d" % (shape, axis))
 
 
+def test_scan_lanes_large():
+    """Interleaved-lane scans of 150-260 MB (thousands of segments per chain):
+    float32 and float64 sums, a ragged lane block, and a product."""
+    import acediar as acd
+    rng = np.random.default_rng(9)
+    for shape, name, op in [((96, 400000), "float", "cumsum"), ((64, 500000), "double", "cumsum"),
+                            ((40, 1000000), "float", "cumprod")]:
+        lo, hi = (0.0, 1.0) if op == "cumsum" else (0.99999, 1.00001)
+        x = rng.uniform(lo, hi, shape).astype(NP[name])
+        got = getattr(acd, op)(acd.as_tensor(x, dtype=name), axis=2).as_array()
+        tol = TOL[name] * (10 if op == "cumprod" else 1)
+        assert_rel(got, oracle.scan(op, x, 1), tol, "%s %s %s" % (op, name, shape))
+
+
 @pytest.mark.parametrize("name", ["float", "double"])
 def test_cumsum_of_view(acd, name):
     rng = np.random.default_rng(4)
