@@ -152,11 +152,20 @@ __device__ __forceinline__ int nonzero_bytes(uint32_t w) {
 // Adds one vector of V elements to a single accumulator: a count over bytes
 // (bool) takes 4 bytes per instruction, everything else element by element
 // (`first` is the index of element 0, used by the argmin/argmax rules).
+// Accumulators that define `static constexpr bool kVecAdd = true` and
+// `add_vec(const Vec<T, V> &)` take a whole vector at once.
+template <class A, class = void>
+struct has_vec_add : std::false_type {};
+template <class A>
+struct has_vec_add<A, std::void_t<decltype(A::kVecAdd)>> : std::integral_constant<bool, A::kVecAdd> {};
+
 template <class Acc, typename T, int V>
 __device__ __forceinline__ void acc_add_vec(Acc &acc, const Vec<T, V> &x, int64_t first) {
   if constexpr (std::is_same<Acc, CountAcc<uint8_t>>::value && V == 16) {
     const uint4 w = *reinterpret_cast<const uint4 *>(&x);
     acc.c += nonzero_bytes(w.x) + nonzero_bytes(w.y) + nonzero_bytes(w.z) + nonzero_bytes(w.w);
+  } else if constexpr (has_vec_add<Acc>::value) {
+    acc.add_vec(x);
   } else {
 #pragma unroll
     for (int k = 0; k < V; ++k) acc.add(x.v[k], first + k);
@@ -343,9 +352,31 @@ struct ArgAcc {
 template <typename T>
 struct SoftStatAcc {
   static constexpr bool kShift = false;
+  static constexpr bool kVecAdd = true;
   double m, s;
   __device__ __forceinline__ void init() { m = -INFINITY; s = 0.0; }
   __device__ __forceinline__ void set_shift(T) {}
+  // A vector at once: one rescale for the vector's maximum, then one exp per
+  // element (the per-element rule below rescales whenever the maximum grows).
+  template <int V>
+  __device__ __forceinline__ void add_vec(const Vec<T, V> &x) {
+    T mb = x.v[0];
+#pragma unroll
+    for (int k = 1; k < V; ++k) mb = m_max(mb, x.v[k]);
+    const double mbd = (double)mb;
+    if (mbd > m) {
+      s = (m == -INFINITY) ? 0.0 : s * exp(m - mbd);
+      m = mbd;
+    }
+    if (m == -INFINITY) {  // only -inf (or NaN) so far: a NaN poisons the sum
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (x.v[k] != x.v[k]) s = (double)NAN;
+      return;
+    }
+#pragma unroll
+    for (int k = 0; k < V; ++k) s += (double)m_exp((T)((double)x.v[k] - m));
+  }
   __device__ __forceinline__ void add(T x, int64_t) {
     const double xd = (double)x;
     if (xd == -INFINITY) return;

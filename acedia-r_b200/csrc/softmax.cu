@@ -654,14 +654,36 @@ static bool launch_softmax_tma(acd_ctx *ctx, const SoftArgs &sa, cudaStream_t s)
 }
 
 // ---- whole tensor ----------------------------------------------------------
-template <typename T, int V>
+template <typename T, int V, int U>
 __global__ void __launch_bounds__(256) k_softmax_apply(T *__restrict__ out, const T *__restrict__ in, int64_t n,
                                                        const double *__restrict__ stats) {
   const T M = (T)stats[0];
   const T inv = (T)(1.0 / stats[1]);
   const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   const int64_t nth = (int64_t)gridDim.x * blockDim.x;
-  for (int64_t i = tid; i < n; i += nth) out[i] = m_exp(in[i] - M) * inv;
+  const bool vec = ((reinterpret_cast<uintptr_t>(in) | reinterpret_cast<uintptr_t>(out)) & 15) == 0;
+  const int64_t nv = vec ? n / V : 0;
+  const Vec<T, V> *iv = reinterpret_cast<const Vec<T, V> *>(in);
+  Vec<T, V> *ov = reinterpret_cast<Vec<T, V> *>(out);
+  int64_t v0 = tid;
+  for (; v0 + (int64_t)(U - 1) * nth < nv; v0 += nth * U) {  // U full vectors: unguarded loads
+    Vec<T, V> x[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) x[u] = iv[v0 + (int64_t)u * nth];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+#pragma unroll
+      for (int k = 0; k < V; ++k) x[u].v[k] = m_exp(x[u].v[k] - M) * inv;
+      ov[v0 + (int64_t)u * nth] = x[u];
+    }
+  }
+  for (; v0 < nv; v0 += nth) {
+    Vec<T, V> x = iv[v0];
+#pragma unroll
+    for (int k = 0; k < V; ++k) x.v[k] = m_exp(x.v[k] - M) * inv;
+    ov[v0] = x;
+  }
+  for (int64_t i = nv * V + tid; i < n; i += nth) out[i] = m_exp(in[i] - M) * inv;
 }
 
 static bool split_axis_sm(const acd_desc *in, const acd_desc *out, int axis, int64_t &L, int64_t &R, int64_t &O,
@@ -791,13 +813,15 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
     acd_status st = f32 ? softmax_stats<float>(ctx, in, s) : softmax_stats<double>(ctx, in, s);
     const double *stats = ctx->control->stats;
     if (st != ACD_OK) return st;
-    const int grid = grid_for(ctx, n, 256, 8);
-    if (f32)
-      k_softmax_apply<float, 4><<<grid, 256, 0, s>>>(reinterpret_cast<float *>(desc_ptr(out)),
-                                                     reinterpret_cast<const float *>(desc_ptr(in)), n, stats);
-    else
-      k_softmax_apply<double, 2><<<grid, 256, 0, s>>>(reinterpret_cast<double *>(desc_ptr(out)),
-                                                      reinterpret_cast<const double *>(desc_ptr(in)), n, stats);
+    if (f32) {
+      const int grid = persistent_grid(ctx, k_softmax_apply<float, 4, 4>, 256, 0, (n / 4 + 1023) / 1024 + 1);
+      k_softmax_apply<float, 4, 4><<<grid, 256, 0, s>>>(reinterpret_cast<float *>(desc_ptr(out)),
+                                                        reinterpret_cast<const float *>(desc_ptr(in)), n, stats);
+    } else {
+      const int grid = persistent_grid(ctx, k_softmax_apply<double, 2, 4>, 256, 0, (n / 2 + 1023) / 1024 + 1);
+      k_softmax_apply<double, 2, 4><<<grid, 256, 0, s>>>(reinterpret_cast<double *>(desc_ptr(out)),
+                                                         reinterpret_cast<const double *>(desc_ptr(in)), n, stats);
+    }
     ACD_CUDA(cudaGetLastError());
     return ACD_OK;
   }
