@@ -374,8 +374,18 @@ struct SoftStatAcc {
         if (x.v[k] != x.v[k]) s = (double)NAN;
       return;
     }
+    // m holds a value of T, so x - m rounded once in T equals the rounding of
+    // the exact difference taken in double; the V exps are summed pairwise in
+    // T (two roundings of a sum of at most V terms <= 1) before one float64 add
+    const T mt = (T)m;
+    T e[V];
 #pragma unroll
-    for (int k = 0; k < V; ++k) s += (double)m_exp((T)((double)x.v[k] - m));
+    for (int k = 0; k < V; ++k) e[k] = m_exp(x.v[k] - mt);
+#pragma unroll
+    for (int w = 1; w < V; w <<= 1)
+#pragma unroll
+      for (int k = 0; k + w < V; k += 2 * w) e[k] += e[k + w];
+    s += (double)e[0];
   }
   __device__ __forceinline__ void add(T x, int64_t) {
     const double xd = (double)x;

@@ -99,11 +99,12 @@ __global__ void __launch_bounds__(256) k_lane_reduce(LaneArgs a) {
 }
 
 // Exclusive scan, in place, of each of `nrows` rows of `nseg` (<= 4096)
-// segment totals: 256 threads x 16 consecutive items.
+// segment totals: 1024 threads x 4 consecutive items (few rows, so the
+// parallelism has to come from within a row).
 template <bool PROD>
-__global__ void __launch_bounds__(256) k_lane_seg_scan(double *seg, int64_t nrows, int nseg) {
-  constexpr int IPT = 16;
-  __shared__ double s_warp[8];
+__global__ void __launch_bounds__(1024) k_lane_seg_scan(double *seg, int64_t nrows, int nseg) {
+  constexpr int IPT = 4, NW = 32;
+  __shared__ double s_warp[NW];
   const double ident = PROD ? 1.0 : 0.0;
   const int wl = threadIdx.x & 31, w = threadIdx.x >> 5;
   const int i0 = threadIdx.x * IPT;
@@ -124,8 +125,19 @@ __global__ void __launch_bounds__(256) k_lane_seg_scan(double *seg, int64_t nrow
     }
     if (wl == 31) s_warp[w] = x;
     __syncthreads();
-    double run = ident;
-    for (int k = 0; k < w; ++k) run = combine<PROD>(run, s_warp[k]);
+    if (w == 0) {  // exclusive scan of the 32 warp totals
+      const double t = s_warp[wl];
+      double u = t;
+#pragma unroll
+      for (int d = 1; d < 32; d <<= 1) {
+        const double y = __shfl_up_sync(0xffffffffu, u, d);
+        if (wl >= d) u = combine<PROD>(y, u);
+      }
+      double e = __shfl_up_sync(0xffffffffu, u, 1);
+      s_warp[wl] = wl == 0 ? ident : e;
+    }
+    __syncthreads();
+    double run = s_warp[w];
     double prev = __shfl_up_sync(0xffffffffu, x, 1);
     if (wl > 0) run = combine<PROD>(run, prev);
 #pragma unroll
@@ -214,7 +226,7 @@ static acd_status launch_lane_scan_lt(acd_ctx *ctx, LaneArgs a, cudaStream_t s) 
         <<<persistent_grid(ctx, k_lane_reduce<T, PROD, LT>, 256, 0, (ntask + 7) / 8), 256, 0, s>>>(a);
     const int64_t nrows = a.nchains * LT;
     const int sg = (int)(nrows < (int64_t)ctx->sm_count * 8 ? nrows : (int64_t)ctx->sm_count * 8);
-    k_lane_seg_scan<PROD><<<sg, 256, 0, s>>>(a.seg, nrows, (int)a.nseg);
+    k_lane_seg_scan<PROD><<<sg, 1024, 0, s>>>(a.seg, nrows, (int)a.nseg);
   }
   k_lane_apply<T, PROD, LT><<<persistent_grid(ctx, k_lane_apply<T, PROD, LT>, 256, 0, (ntask + 7) / 8), 256, 0, s>>>(a);
   return ACD_OK;
