@@ -85,6 +85,7 @@ def _bind(lib):
         "acd_scalar": ([vp, i32, dp, dp, f64, vp], i32),
         "acd_fused": ([vp, i32, dp, dp, dp, f64, vp], i32),
         "acd_copy": ([vp, dp, dp, vp], i32),
+        "acd_convert": ([vp, dp, dp, vp], i32),
         "acd_reduce": ([vp, i32, dp, dp, u32, vp], i32),
         "acd_sum_var": ([vp, dp, dp, dp, vp], i32),
         "acd_arg_reduce": ([vp, i32, dp, dp, dp, i32, i32, vp], i32),

@@ -322,6 +322,24 @@ def is_contiguous(x):
     return x.is_contiguous()
 
 
+_DTYPE_ALIASES = {"float32": "float", "float": "float", "float64": "double", "double": "double",
+                  "int32": "int32", "int": "int32", "int64": "int64", "long": "int64", "bool": "bool",
+                  "logical": "bool"}
+
+
+def to_dtype(x, target_dtype):
+    """tensor_to_dtype_unified (src/TensorDataAccess.cpp:152-190): a new tensor
+    of `target_dtype` holding as.<dtype>(x) (truncation toward zero and NA for
+    NaN or out-of-range values when converting to an integer type)."""
+    dt = _DTYPE_ALIASES.get(target_dtype)
+    if dt is None:
+        raise ValueError("Error converting tensor dtype: Unsupported target dtype: %s" % target_dtype)
+    out = _alloc(x.shape, dt, x.device)
+    L.check(L.lib().acd_convert(context(), ctypes.byref(out.desc()), ctypes.byref(x.desc()), _stream()),
+            "to_dtype")
+    return out
+
+
 def view(x, shape):
     shape = tuple(int(s) for s in shape)
     if int(np.prod(shape)) != x.size:

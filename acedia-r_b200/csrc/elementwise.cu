@@ -546,11 +546,46 @@ static acd_status scalar_to(acd_ctx *ctx, int op, const acd_desc *out, const acd
 
 static bool is_compare(int op) { return op >= ACD_GT && op <= ACD_LE; }
 
+template <typename From>
+static acd_status convert_from(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, cudaStream_t s) {
+  const int64_t *st = in->stride;
+  switch (out->dtype) {
+    case ACD_FLOAT32: return launch_map(ctx, ConvertF<From, float>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_FLOAT64: return launch_map(ctx, ConvertF<From, double>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_INT32: return launch_map(ctx, ConvertF<From, int32_t>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_INT64: return launch_map(ctx, ConvertF<From, int64_t>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_BOOL: return launch_map(ctx, ConvertF<From, uint8_t>{}, out, in, st, nullptr, nullptr, s);
+    default: return fail(ACD_ERR_DTYPE, "acd_convert: target dtype %d not supported", out->dtype);
+  }
+}
+
 }  // namespace acd
 
 using namespace acd;
 
 extern "C" {
+
+acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_convert: null context");
+  ACD_TRY(check_desc(out, "out"));
+  ACD_TRY(check_desc(in, "in"));
+  ACD_TRY(same_shape(out, in, "acd_convert"));
+  if (out->dtype == in->dtype) return acd_copy(ctx, out, in, stream);
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  switch (in->dtype) {
+    case ACD_FLOAT32: st = convert_from<float>(ctx, out, in, s); break;
+    case ACD_FLOAT64: st = convert_from<double>(ctx, out, in, s); break;
+    case ACD_INT32: st = convert_from<int32_t>(ctx, out, in, s); break;
+    case ACD_INT64: st = convert_from<int64_t>(ctx, out, in, s); break;
+    case ACD_BOOL: st = convert_from<uint8_t>(ctx, out, in, s); break;
+    default: return fail(ACD_ERR_DTYPE, "acd_convert: source dtype %d not supported", in->dtype);
+  }
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
 
 acd_status acd_unary(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, acd_stream stream) {
   if (!ctx) return fail(ACD_ERR_INVALID, "acd_unary: null context");

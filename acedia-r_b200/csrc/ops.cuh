@@ -12,6 +12,9 @@
 // is x*x.
 #pragma once
 
+#include <climits>
+#include <type_traits>
+
 #include "common.cuh"
 
 namespace acd {
@@ -132,6 +135,50 @@ struct SquareScalarF {
   using In = T;
   using Out = T;
   __device__ __forceinline__ T operator()(T a) const { return a * a; }
+};
+
+// ---- dtype conversion ------------------------------------------------------
+// Base R's as.* rules on tensor storage: to an integer type a value is
+// truncated toward zero, and NaN or a value outside the type's range becomes
+// NA (INT32_MIN for int32, INT64_MIN for int64); an NA integer becomes NaN in
+// a floating type; float <-> double and int64 -> float round to nearest;
+// bool stores x != 0 (bool has no NA, so NaN and NA integers become 1).
+template <typename From, typename To>
+__device__ __forceinline__ To convert_value(From x) {
+  if constexpr (std::is_same<From, To>::value) {
+    return x;
+  } else if constexpr (std::is_same<To, uint8_t>::value) {
+    return (uint8_t)(x != From(0));
+  } else if constexpr (std::is_floating_point<To>::value) {
+    if constexpr (std::is_same<From, int32_t>::value)
+      return x == INT32_MIN ? To(NAN) : (To)x;
+    else if constexpr (std::is_same<From, int64_t>::value)
+      return x == INT64_MIN ? To(NAN) : (To)x;
+    else
+      return (To)x;
+  } else if constexpr (std::is_same<To, int32_t>::value) {
+    if constexpr (std::is_floating_point<From>::value)
+      return (x > (From)-2147483648.0 && x < (From)2147483648.0) ? (int32_t)x : INT32_MIN;
+    else if constexpr (std::is_same<From, int64_t>::value)
+      return (x >= -2147483647LL && x <= 2147483647LL) ? (int32_t)x : INT32_MIN;
+    else
+      return (int32_t)x;
+  } else {
+    if constexpr (std::is_floating_point<From>::value)
+      return (x > (From)-9223372036854775808.0 && x < (From)9223372036854775808.0) ? (int64_t)x : INT64_MIN;
+    else if constexpr (std::is_same<From, int32_t>::value)
+      return x == INT32_MIN ? INT64_MIN : (int64_t)x;
+    else
+      return (int64_t)x;
+  }
+}
+
+template <typename From, typename To>
+struct ConvertF {
+  static constexpr int kIn = 1;
+  using In = From;
+  using Out = To;
+  __device__ __forceinline__ To operator()(From x) const { return convert_value<From, To>(x); }
 };
 
 // ---- fused chains ----------------------------------------------------------

@@ -321,6 +321,8 @@ def run_config_report(a):
             ops.append(_op("%s(T)" % op, (lambda op=op: getattr(acd, "tensor_" + op)(T)), B, peak))
         ops.append(_op("sum+var fused", lambda: acd.sum_var(T), B, peak, note="includes two 8-byte D2H reads"))
         ops.append(_op("which.max(T)", lambda: Tm._arg("argmax", T), B, peak))
+        ops.append(_op("as.double(T)", lambda: acd.to_dtype(T, "double"), B + 2 * B, peak, graph=True))
+        ops.append(_op("as.integer(T)", lambda: acd.to_dtype(T, "int32"), 2 * B, peak, graph=True))
         for ax in (1, 2, 3):
             kept = n // shp[ax - 1]
             for op in ("sum", "mean", "var", "max"):

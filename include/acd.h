@@ -163,6 +163,15 @@ acd_status acd_scalar(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
 /* Fused chains (acd_fused_op).  `b` is NULL for one-input chains. */
 acd_status acd_fused(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *a,
                      const acd_desc *b, double p0, acd_stream stream);
+/* dtype conversion, out = as.<dtype>(in) over any two views of one shape.
+ * Replaces tensor_to_dtype_unified (src/TensorDataAccess.cpp:152-190), whose
+ * kernel is type_conversion_kernel (src/kernels/tensor_kernels.cu:52-57,
+ * a static_cast per element, src/kernels/kernel_utils.cuh:11).  Base R's
+ * as.* rules: to int32/int64 values truncate toward zero and NaN or values
+ * out of range become NA (INT32_MIN / INT64_MIN); NA integers become NaN in
+ * float32/float64; bool stores x != 0.  Equal dtypes copy. */
+acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream);
+
 /* out = in, any strides on both sides (contiguous(), strided copy). */
 acd_status acd_copy(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream);
 

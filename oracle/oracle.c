@@ -226,6 +226,73 @@ void orc_copy(int dt, const void *in, int nd, const int64_t *shape, const int64_
   orc_unary(U_COPY, dt, in, nd, shape, st, out);
 }
 
+/* ---- dtype conversion: base R's as.* rules -------------------------------
+ * (the reference converts with a static_cast per element,
+ * src/kernels/tensor_kernels.cu:52-57 and src/kernels/kernel_utils.cuh:11;
+ * R's as.integer truncates toward zero and gives NA for NaN and out-of-range
+ * values; NA integers are INT32_MIN / INT64_MIN and convert to NaN). */
+static void convert_one(int from, int to, const void *in, int64_t off, void *out, int64_t i) {
+  if (to == DT_F32 || to == DT_F64) {
+    long double v;
+    if (from == DT_I32) {
+      const int32_t x = ((const int32_t *)in)[off];
+      v = x == INT32_MIN ? (long double)NAN : (long double)x;
+    } else if (from == DT_I64) {
+      const int64_t x = ((const int64_t *)in)[off];
+      v = x == INT64_MIN ? (long double)NAN : (long double)x; /* exact in long double */
+    } else {
+      v = ld_get(in, from, off);
+    }
+    if (to == DT_F32)
+      ((float *)out)[i] = (float)v; /* one rounding: v holds the source value exactly */
+    else
+      ((double *)out)[i] = (double)v;
+  } else if (to == DT_I32) {
+    int32_t r;
+    if (from == DT_F32 || from == DT_F64) {
+      const long double x = ld_get(in, from, off);
+      r = (x > -2147483648.0L && x < 2147483648.0L) ? (int32_t)truncl(x) : INT32_MIN;
+    } else if (from == DT_I64) {
+      const int64_t x = ((const int64_t *)in)[off];
+      r = (x >= -2147483647LL && x <= 2147483647LL) ? (int32_t)x : INT32_MIN;
+    } else if (from == DT_BOOL) {
+      r = ((const uint8_t *)in)[off];
+    } else {
+      r = ((const int32_t *)in)[off];
+    }
+    ((int32_t *)out)[i] = r;
+  } else if (to == DT_I64) {
+    int64_t r;
+    if (from == DT_F32 || from == DT_F64) {
+      const long double x = ld_get(in, from, off);
+      r = (x > -9223372036854775808.0L && x < 9223372036854775808.0L) ? (int64_t)truncl(x) : INT64_MIN;
+    } else if (from == DT_I32) {
+      const int32_t x = ((const int32_t *)in)[off];
+      r = x == INT32_MIN ? INT64_MIN : (int64_t)x;
+    } else if (from == DT_BOOL) {
+      r = ((const uint8_t *)in)[off];
+    } else {
+      r = ((const int64_t *)in)[off];
+    }
+    ((int64_t *)out)[i] = r;
+  } else { /* bool: x != 0, so NaN and NA integers give 1 */
+    int nz;
+    switch (from) {
+      case DT_F32: nz = ((const float *)in)[off] != 0.0f; break;
+      case DT_F64: nz = ((const double *)in)[off] != 0.0; break;
+      case DT_I32: nz = ((const int32_t *)in)[off] != 0; break;
+      case DT_I64: nz = ((const int64_t *)in)[off] != 0; break;
+      default: nz = ((const uint8_t *)in)[off] != 0; break;
+    }
+    ((uint8_t *)out)[i] = (uint8_t)nz;
+  }
+}
+
+void orc_convert(int from, int to, const void *in, int nd, const int64_t *shape, const int64_t *st, void *out) {
+  const int64_t n = numel(nd, shape);
+  for (int64_t i = 0; i < n; ++i) convert_one(from, to, in, offset_of(i, nd, shape, st), out, i);
+}
+
 /* ---- reductions over a set of reduced values ---------------------------- */
 static long double r_mean(const long double *v, int64_t n) {
   long double s = 0.0L;

@@ -166,6 +166,18 @@ def scalar(op, x, s, out_dtype=None):
     return _result(out, v.shape)
 
 
+def convert(x, to_dtype):
+    """as.<dtype>(x): to_dtype is a numpy dtype (float32, float64, int32, int64, bool)."""
+    v = View.of(x)
+    to = np.dtype(to_dtype)
+    out = np.empty(int(np.prod(v.shape)), dtype=np.uint8 if to == np.bool_ else to)
+    lib().orc_convert(DT[v.dtype], DT[to], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
+                      out.ctypes.data_as(ctypes.c_void_p))
+    if to == np.bool_:
+        out = out.view(np.bool_)
+    return _result(out, v.shape)
+
+
 def gauss_chain(x, p=0.5):
     """x*p + exp(-(x^2)) with one rounding per R operator."""
     a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))
