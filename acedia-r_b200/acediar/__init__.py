@@ -9,4 +9,5 @@ from .tensor import (  # noqa: F401
     cumprod, cumsum, dtype, empty_tensor, erf, exp, floor, from_torch, fused, gpu_tensor, gpuTensor, is_contiguous,
     log, max, mean, min, permute_view, pmax, pmin, prod, relu, reshape, round, shape, sigmoid, sin, softmax, sqrt,
     sum, sum_var, synchronize, tanh, tensor_count, tensor_max, tensor_mean, tensor_min, tensor_prod, tensor_sum,
-    tensor_var, to_dtype, transpose, transpose_view, var, view, which_max, which_min)
+    tensor_var, to_dtype, transpose, transpose_view, var, view, which_max, which_min, subset, assign, concat,
+    concat_tensor, stack, stack_tensor, repeat_tensor, pad, pad_tensor)

@@ -86,6 +86,13 @@ def _bind(lib):
         "acd_fused": ([vp, i32, dp, dp, dp, f64, vp], i32),
         "acd_copy": ([vp, dp, dp, vp], i32),
         "acd_convert": ([vp, dp, dp, vp], i32),
+        "acd_slice_desc": ([dp, P(i64), P(i64), dp], i32),
+        "acd_fill": ([vp, dp, ctypes.c_double, vp], i32),
+        "acd_mask_fill": ([vp, dp, dp, ctypes.c_double, vp], i32),
+        "acd_concat": ([vp, dp, ctypes.POINTER(dp), i32, i32, vp], i32),
+        "acd_stack": ([vp, dp, ctypes.POINTER(dp), i32, i32, vp], i32),
+        "acd_repeat": ([vp, dp, dp, P(i64), vp], i32),
+        "acd_pad": ([vp, dp, dp, P(i64), i32, ctypes.c_double, vp], i32),
         "acd_reduce": ([vp, i32, dp, dp, u32, vp], i32),
         "acd_sum_var": ([vp, dp, dp, dp, vp], i32),
         "acd_arg_reduce": ([vp, i32, dp, dp, dp, i32, i32, vp], i32),

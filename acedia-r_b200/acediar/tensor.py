@@ -322,6 +322,179 @@ def is_contiguous(x):
     return x.is_contiguous()
 
 
+# ---- slicing, assignment and assembly (src/TensorMutation.cpp) -------------
+def _ranges(x, idx, what):
+    """R index arguments -> (start0, count, keep) per axis.  None selects the
+    whole axis, an int (1-based) one element (the axis is dropped), a
+    sequence of 1-based ints a contiguous range (R/gpuTensor.R:719-811)."""
+    if len(idx) > x.ndims:
+        raise ValueError("Too many indices for tensor with %d dimensions" % x.ndims)
+    starts, counts, keep = [], [], []
+    for d in range(x.ndims):
+        i = idx[d] if d < len(idx) else None
+        n = x.shape[d]
+        if i is None:
+            starts.append(0), counts.append(n), keep.append(True)
+            continue
+        v = [int(i)] if isinstance(i, numbers.Number) else [int(k) for k in i]
+        if any(k <= 0 for k in v):
+            raise ValueError("Only positive indices are supported in this implementation" if what == "[" else
+                             "Negative or zero indices not supported in slice assignment")
+        if any(k > n for k in v):
+            raise ValueError("Index %d is out of bounds for dimension %d with size %d" % (builtins.max(v), d + 1, n)
+                             if what == "[" else "Index out of bounds in slice assignment")
+        if any(b - a != 1 for a, b in zip(v, v[1:])):
+            raise ValueError("Only contiguous ranges are supported in this basic implementation" if what == "[" else
+                             "Only contiguous ranges supported in slice assignment")
+        starts.append(v[0] - 1), counts.append(len(v)), keep.append(len(v) > 1 or not isinstance(i, numbers.Number))
+    return starts, counts, keep
+
+
+def _slice_view(x, starts, counts):
+    st = (ctypes.c_int64 * builtins.max(x.ndims, 1))(*starts)
+    ct = (ctypes.c_int64 * builtins.max(x.ndims, 1))(*counts)
+    d = L.Desc()
+    L.check(L.lib().acd_slice_desc(ctypes.byref(x.desc()), st, ct, ctypes.byref(d)), "slice")
+    return gpuTensor(x.storage, tuple(counts), x.dtype, x.strides, d.offset)
+
+
+def subset(x, *idx):
+    """`[.gpuTensor`: x[i, j, ...] with R's 1-based contiguous ranges; a
+    single index drops its axis, and a result with no axes left is a
+    number (R/gpuTensor.R:719-811)."""
+    if not idx:
+        return x
+    starts, counts, keep = _ranges(x, idx, "[")
+    v = contiguous(_slice_view(x, starts, counts))
+    new_shape = [c for c, k in zip(counts, keep) if k]
+    if not new_shape:
+        return _scalar_result(v)
+    return gpuTensor(v.storage, tuple(new_shape), v.dtype, col_major_strides(new_shape), v.offset)
+
+
+def assign(x, *idx, value):
+    """`[<-.gpuTensor`, in place: x[mask] <- scalar (mask a bool tensor or a
+    logical array of x's length), x[ranges] <- scalar, x[ranges] <- tensor or
+    vector of the slice's shape (src/TensorMutation.cpp:439-623)."""
+    if len(idx) == 1 and (isinstance(idx[0], gpuTensor) and idx[0].dtype == "bool" or
+                          isinstance(idx[0], np.ndarray) and idx[0].dtype == np.bool_):
+        m = idx[0]
+        if isinstance(m, np.ndarray):
+            if m.size != x.size:
+                raise ValueError("Logical mask must have same length as tensor")
+            m = as_tensor(m.reshape(x.shape if x.shape else (1,), order="F"), dtype="bool")
+        if not isinstance(value, numbers.Number):
+            raise ValueError("Currently only scalar assignment to boolean mask is supported")
+        L.check(L.lib().acd_mask_fill(context(), ctypes.byref(x.desc()), ctypes.byref(m.desc()),
+                                      ctypes.c_double(float(value)), _stream()), "mask assignment")
+        return x
+    starts, counts, _ = _ranges(x, idx, "[<-")
+    v = _slice_view(x, starts, counts)
+    if isinstance(value, numbers.Number):
+        L.check(L.lib().acd_fill(context(), ctypes.byref(v.desc()), ctypes.c_double(float(value)), _stream()),
+                "slice assignment")
+        return x
+    if not isinstance(value, gpuTensor):
+        value = as_tensor(np.asarray(value).reshape(counts, order="F"), dtype=x.dtype)
+    if value.dtype != x.dtype:
+        value = to_dtype(value, x.dtype)
+    if value.size != v.size:
+        raise ValueError("Source tensor shape must match slice shape")
+    src = value if tuple(value.shape) == tuple(counts) else gpuTensor(
+        contiguous(value).storage, tuple(counts), value.dtype)
+    L.check(L.lib().acd_copy(context(), ctypes.byref(v.desc()), ctypes.byref(src.desc()), _stream()),
+            "slice assignment")
+    return x
+
+
+def _desc_array(tensors):
+    descs = [t.desc() for t in tensors]
+    arr = (ctypes.POINTER(L.Desc) * len(descs))(*[ctypes.pointer(d) for d in descs])
+    return arr, descs
+
+
+def concat_tensor(lst, axis=1):
+    """tensor_concat_unified (src/TensorMutation.cpp:167-273): concatenation
+    along `axis` (1-based)."""
+    if len(lst) < 2:
+        raise ValueError("Need at least two tensors to concatenate")
+    a = int(axis) - 1
+    base = lst[0]
+    if a < 0 or a >= base.ndims:
+        raise ValueError("axis out of range")
+    shape = list(base.shape)
+    shape[a] = builtins.sum(t.shape[a] for t in lst) if all(t.ndims == base.ndims for t in lst) else -1
+    if shape[a] < 0:
+        raise ValueError("All tensors must have same number of dims")
+    out = _alloc(tuple(shape), base.dtype, base.device)
+    arr, keep = _desc_array(lst)
+    L.check(L.lib().acd_concat(context(), ctypes.byref(out.desc()), arr, len(lst), a, _stream()), "concat")
+    return out
+
+
+def stack_tensor(lst, axis=1):
+    """tensor_stack_unified (src/TensorMutation.cpp:275-331): equal-shaped
+    tensors stacked along a new axis at position `axis` (1-based)."""
+    if len(lst) < 2:
+        raise ValueError("Need at least two tensors to stack")
+    a = int(axis) - 1
+    base = lst[0]
+    if a < 0 or a > base.ndims:
+        raise ValueError("axis out of range")
+    shape = list(base.shape)
+    shape.insert(a, len(lst))
+    out = _alloc(tuple(shape), base.dtype, base.device)
+    arr, keep = _desc_array(lst)
+    L.check(L.lib().acd_stack(context(), ctypes.byref(out.desc()), arr, len(lst), a, _stream()), "stack")
+    return out
+
+
+def repeat_tensor(x, reps):
+    """tensor_repeat_unified (src/TensorMutation.cpp:333-385): each element
+    repeated reps[d] times along axis d."""
+    reps = [int(r) for r in (reps if not isinstance(reps, numbers.Number) else [reps])]
+    if len(reps) != x.ndims:
+        raise ValueError("repeats length must match tensor dims")
+    if any(r <= 0 for r in reps):
+        raise ValueError("repeat counts must be positive")
+    out = _alloc(tuple(s * r for s, r in zip(x.shape, reps)), x.dtype, x.device)
+    rp = (ctypes.c_int64 * len(reps))(*reps)
+    L.check(L.lib().acd_repeat(context(), ctypes.byref(out.desc()), ctypes.byref(x.desc()), rp, _stream()), "repeat")
+    return out
+
+
+_PAD_MODES = {"constant": 0, "reflect": 1, "replicate": 2}
+
+
+def pad(x, pad_width, mode="constant", value=0):
+    """tensor_pad_unified (src/TensorMutation.cpp:387-437): pad_width is an
+    ndims x 2 matrix of (before, after) counts."""
+    if mode not in _PAD_MODES:
+        raise ValueError("Unsupported pad mode")
+    pw = np.asarray(pad_width, dtype=np.int64).reshape(-1, 2)
+    if pw.shape[0] != x.ndims:
+        raise ValueError("pad_width must be matrix of ndims x 2")
+    if (pw < 0).any():
+        raise ValueError("padding must be non-negative")
+    out = _alloc(tuple(int(s + b + a) for s, (b, a) in zip(x.shape, pw)), x.dtype, x.device)
+    bp = (ctypes.c_int64 * x.ndims)(*[int(b) for b in pw[:, 0]])
+    L.check(L.lib().acd_pad(context(), ctypes.byref(out.desc()), ctypes.byref(x.desc()), bp, _PAD_MODES[mode],
+                            ctypes.c_double(float(value)), _stream()), "pad")
+    return out
+
+
+def pad_tensor(x, pad_width, mode="constant", value=0):
+    """pad_tensor (R/gpuTensor.R:1816-1831): pad_width = c(before1, after1,
+    before2, after2, ...)."""
+    if len(pad_width) != x.ndims * 2:
+        raise ValueError("pad_width must have length ndims * 2")
+    return pad(x, np.asarray(pad_width).reshape(x.ndims, 2), mode, value)
+
+
+concat = concat_tensor
+stack = stack_tensor
+
+
 _DTYPE_ALIASES = {"float32": "float", "float": "float", "float64": "double", "double": "double",
                   "int32": "int32", "int": "int32", "int64": "int64", "long": "int64", "bool": "bool",
                   "logical": "bool"}

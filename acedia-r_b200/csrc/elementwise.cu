@@ -546,6 +546,117 @@ static acd_status scalar_to(acd_ctx *ctx, int op, const acd_desc *out, const acd
 
 static bool is_compare(int op) { return op >= ACD_GT && op <= ACD_LE; }
 
+// out = v for every element of a view.  The launcher wants one input operand:
+// it is the output's first element at stride 0 on every axis, never read.
+template <typename T>
+struct FillF {
+  static constexpr int kIn = 1;
+  using In = T;
+  using Out = T;
+  T v;
+  __device__ __forceinline__ T operator()(T) const { return v; }
+};
+
+template <typename T>
+static acd_status fill_t(acd_ctx *ctx, const acd_desc *out, double value, cudaStream_t s) {
+  int64_t zero[ACD_MAX_DIMS] = {0, 0, 0, 0, 0, 0, 0, 0};
+  return launch_map(ctx, FillF<T>{convert_value<double, T>(value)}, out, out, zero, nullptr, nullptr, s);
+}
+
+// x[i] = v where mask[i] != 0, in place.  Dense operands take 16 mask bytes
+// per load; other views walk int64 coordinates in runs of 4.
+template <typename T>
+__global__ void __launch_bounds__(kEwThreads) k_mask_fill_flat(T *__restrict__ x, const uint8_t *__restrict__ m,
+                                                               int64_t n, T v) {
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  const int64_t nv = (reinterpret_cast<uintptr_t>(m) & 15) == 0 ? n / 16 : 0;
+  for (int64_t i = tid; i < nv; i += nth) {
+    const uint4 w = reinterpret_cast<const uint4 *>(m)[i];
+    const uint32_t ws[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+    for (int q = 0; q < 4; ++q)
+      if (ws[q])
+#pragma unroll
+        for (int b = 0; b < 4; ++b)
+          if ((ws[q] >> (8 * b)) & 0xffu) x[i * 16 + q * 4 + b] = v;
+  }
+  for (int64_t i = nv * 16 + tid; i < n; i += nth)
+    if (m[i]) x[i] = v;
+}
+
+template <typename T>
+__global__ void __launch_bounds__(kEwThreads) k_mask_fill_general(T *__restrict__ x, const uint8_t *__restrict__ m,
+                                                                  GenSpace g, int64_t n, T v) {
+  constexpr int RUN = 4;
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t base = tid * RUN; base < n; base += nth * RUN) {
+    int64_t c[ACD_MAX_DIMS];
+    int64_t ox = 0, om = 0, rem = base;
+#pragma unroll
+    for (int d = 0; d < ACD_MAX_DIMS; ++d) {
+      if (d < g.ndim) {
+        c[d] = rem % g.shape[d];
+        rem /= g.shape[d];
+        ox += c[d] * g.st[0][d];
+        om += c[d] * g.st[1][d];
+      }
+    }
+    for (int r = 0; r < RUN && base + r < n; ++r) {
+      if (m[om]) x[ox] = v;
+      ox += g.st[0][0];
+      om += g.st[1][0];
+      if (++c[0] == g.shape[0]) {
+        c[0] = 0;
+        ox -= g.shape[0] * g.st[0][0];
+        om -= g.shape[0] * g.st[1][0];
+        for (int d = 1; d < g.ndim; ++d) {
+          ox += g.st[0][d];
+          om += g.st[1][d];
+          if (++c[d] < g.shape[d]) break;
+          c[d] = 0;
+          ox -= g.shape[d] * g.st[0][d];
+          om -= g.shape[d] * g.st[1][d];
+        }
+      }
+    }
+  }
+}
+
+template <typename T>
+static acd_status mask_fill_t(acd_ctx *ctx, const acd_desc *x, const acd_desc *mask, double value,
+                              cudaStream_t s) {
+  IterSpace it;
+  it.ndim = x->ndim;
+  it.nops = 2;
+  for (int d = 0; d < x->ndim; ++d) {
+    it.shape[d] = x->shape[d];
+    it.stride[0][d] = x->stride[d];
+    it.stride[1][d] = mask->stride[d];
+  }
+  const int64_t n = it.numel();
+  if (n == 0) return ACD_OK;
+  collapse(it);
+  T *px = reinterpret_cast<T *>(desc_ptr(x));
+  const uint8_t *pm = reinterpret_cast<const uint8_t *>(desc_ptr(mask));
+  const T v = convert_value<double, T>(value);
+  if (it.ndim == 1 && it.stride[0][0] == 1 && it.stride[1][0] == 1) {
+    const int grid = persistent_grid(ctx, k_mask_fill_flat<T>, kEwThreads, 0, (n / 16 + kEwThreads) / kEwThreads);
+    k_mask_fill_flat<T><<<grid, kEwThreads, 0, s>>>(px, pm, n, v);
+    return ACD_OK;
+  }
+  GenSpace g;
+  g.ndim = it.ndim;
+  for (int d = 0; d < ACD_MAX_DIMS; ++d) {
+    g.shape[d] = d < it.ndim ? it.shape[d] : 1;
+    for (int o = 0; o < kMaxOps; ++o) g.st[o][d] = (d < it.ndim && o < 2) ? it.stride[o][d] : 0;
+  }
+  const int grid = persistent_grid(ctx, k_mask_fill_general<T>, kEwThreads, 0, ((n + 3) / 4 + kEwThreads - 1) / kEwThreads);
+  k_mask_fill_general<T><<<grid, kEwThreads, 0, s>>>(px, pm, g, n, v);
+  return ACD_OK;
+}
+
 template <typename From>
 static acd_status convert_from(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, cudaStream_t s) {
   const int64_t *st = in->stride;
@@ -581,6 +692,48 @@ acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, ac
     case ACD_INT64: st = convert_from<int64_t>(ctx, out, in, s); break;
     case ACD_BOOL: st = convert_from<uint8_t>(ctx, out, in, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_convert: source dtype %d not supported", in->dtype);
+  }
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_fill(acd_ctx *ctx, const acd_desc *out, double value, acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_fill: null context");
+  ACD_TRY(check_desc(out, "out"));
+  if (desc_numel(out) == 0) return ACD_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  switch (out->dtype) {
+    case ACD_FLOAT32: st = fill_t<float>(ctx, out, value, s); break;
+    case ACD_FLOAT64: st = fill_t<double>(ctx, out, value, s); break;
+    case ACD_INT32: st = fill_t<int32_t>(ctx, out, value, s); break;
+    case ACD_INT64: st = fill_t<int64_t>(ctx, out, value, s); break;
+    case ACD_BOOL: st = fill_t<uint8_t>(ctx, out, value, s); break;
+    default: return fail(ACD_ERR_DTYPE, "acd_fill: dtype %d not supported", out->dtype);
+  }
+  if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_mask_fill(acd_ctx *ctx, const acd_desc *x, const acd_desc *mask, double value, acd_stream stream) {
+  if (!ctx) return fail(ACD_ERR_INVALID, "acd_mask_fill: null context");
+  ACD_TRY(check_desc(x, "x"));
+  ACD_TRY(check_desc(mask, "mask"));
+  if (mask->dtype != ACD_BOOL) return fail(ACD_ERR_DTYPE, "Mask tensor must be boolean type");
+  if (same_shape(x, mask, "acd_mask_fill") != ACD_OK) return fail(ACD_ERR_SHAPE, "Tensor and mask must have the same shape");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  acd_status st;
+  switch (x->dtype) {
+    case ACD_FLOAT32: st = mask_fill_t<float>(ctx, x, mask, value, s); break;
+    case ACD_FLOAT64: st = mask_fill_t<double>(ctx, x, mask, value, s); break;
+    case ACD_INT32: st = mask_fill_t<int32_t>(ctx, x, mask, value, s); break;
+    case ACD_INT64: st = mask_fill_t<int64_t>(ctx, x, mask, value, s); break;
+    case ACD_BOOL: st = mask_fill_t<uint8_t>(ctx, x, mask, value, s); break;
+    default: return fail(ACD_ERR_DTYPE, "acd_mask_fill: dtype %d not supported", x->dtype);
   }
   if (st != ACD_OK) return st;
   ACD_CUDA(cudaGetLastError());

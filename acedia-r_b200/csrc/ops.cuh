@@ -144,7 +144,7 @@ struct SquareScalarF {
 // a floating type; float <-> double and int64 -> float round to nearest;
 // bool stores x != 0 (bool has no NA, so NaN and NA integers become 1).
 template <typename From, typename To>
-__device__ __forceinline__ To convert_value(From x) {
+__host__ __device__ __forceinline__ To convert_value(From x) {
   if constexpr (std::is_same<From, To>::value) {
     return x;
   } else if constexpr (std::is_same<To, uint8_t>::value) {

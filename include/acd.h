@@ -163,6 +163,43 @@ acd_status acd_scalar(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
 /* Fused chains (acd_fused_op).  `b` is NULL for one-input chains. */
 acd_status acd_fused(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *a,
                      const acd_desc *b, double p0, acd_stream stream);
+/* ---- assembly and mutation (views of acd_desc) ------------------------- */
+/* Host only: the view of `in` restricted to start[d] .. start[d]+count[d]-1
+ * (0-based) on every axis, same rank.  `[.gpuTensor` (R/gpuTensor.R:719-811)
+ * extracts such ranges by a host round trip; here the view is zero-copy and
+ * acd_copy materialises it. */
+acd_status acd_slice_desc(const acd_desc *in, const int64_t *start, const int64_t *count, acd_desc *out);
+/* out = value on every element of a view (value converted as by acd_convert).
+ * With acd_slice_desc this is tensor_slice_set_scalar_unified
+ * (src/TensorMutation.cpp:439-492, src/kernels/tensor_slice_update.cu). */
+acd_status acd_fill(acd_ctx *ctx, const acd_desc *out, double value, acd_stream stream);
+/* x[mask] <- value in place; mask is a bool view of x's shape.
+ * Replaces tensor_mask_set_scalar_unified (src/TensorMutation.cpp:577-623). */
+acd_status acd_mask_fill(acd_ctx *ctx, const acd_desc *x, const acd_desc *mask, double value,
+                         acd_stream stream);
+/* out = concatenation of ins[0..n-1] along `axis` (0-based); every other
+ * extent equal.  Replaces tensor_concat_unified (src/TensorMutation.cpp:167-273,
+ * concat_kernel src/kernels/tensor_kernels.cu:298-341). */
+acd_status acd_concat(acd_ctx *ctx, const acd_desc *out, const acd_desc *const *ins, int32_t n, int32_t axis,
+                      acd_stream stream);
+/* out = the n equal-shaped inputs stacked along a new axis `axis` (0-based,
+ * 0..rank).  Replaces tensor_stack_unified (src/TensorMutation.cpp:275-331). */
+acd_status acd_stack(acd_ctx *ctx, const acd_desc *out, const acd_desc *const *ins, int32_t n, int32_t axis,
+                     acd_stream stream);
+/* out(c) = in(c / reps) per axis: every element repeated reps[d] times along
+ * axis d.  Replaces tensor_repeat_unified (src/TensorMutation.cpp:333-385,
+ * repeat_kernel src/kernels/tensor_kernels.cu:381-413). */
+acd_status acd_repeat(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, const int64_t *reps,
+                      acd_stream stream);
+/* out = in padded by before[d] elements in front and
+ * out.shape[d] - in.shape[d] - before[d] behind on each axis.  mode 0:
+ * `value`; 1: reflect with the edge included (the reference's rule, padding
+ * at most the axis length); 2: replicate the edge.  Replaces
+ * tensor_pad_unified (src/TensorMutation.cpp:387-437, pad_kernel
+ * src/kernels/tensor_kernels.cu:415-466). */
+acd_status acd_pad(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, const int64_t *before, int32_t mode,
+                   double value, acd_stream stream);
+
 /* dtype conversion, out = as.<dtype>(in) over any two views of one shape.
  * Replaces tensor_to_dtype_unified (src/TensorDataAccess.cpp:152-190), whose
  * kernel is type_conversion_kernel (src/kernels/tensor_kernels.cu:52-57,

@@ -178,6 +178,40 @@ def convert(x, to_dtype):
     return _result(out, v.shape)
 
 
+# ---- assembly (pure data movement, restated with numpy on logical arrays) ----
+def concat(arrays, axis):
+    """concat_kernel (src/kernels/tensor_kernels.cu:298-341): the inputs in
+    order along `axis` (0-based)."""
+    return np.concatenate([np.asarray(a) for a in arrays], axis=axis)
+
+
+def stack(arrays, axis):
+    """stack_kernel (src/kernels/tensor_kernels.cu:343-379): a new axis at
+    position `axis` (0-based) indexing the inputs."""
+    return np.stack([np.asarray(a) for a in arrays], axis=axis)
+
+
+def repeat(x, reps):
+    """repeat_kernel (src/kernels/tensor_kernels.cu:381-413): out(c) =
+    in(c // reps) on every axis."""
+    x = np.asarray(x)
+    for d, r in enumerate(reps):
+        x = np.repeat(x, int(r), axis=d)
+    return x
+
+
+def pad(x, before, after, mode="constant", value=0.0):
+    """pad_kernel (src/kernels/tensor_kernels.cu:415-466): constant, reflect
+    with the edge included (numpy's "symmetric"), replicate ("edge").  The
+    constant is converted to the tensor dtype as as.<dtype> would."""
+    x = np.asarray(x)
+    width = [(int(b), int(a)) for b, a in zip(before, after)]
+    if mode == "constant":
+        v = convert(np.array([value], dtype=np.float64), x.dtype if x.dtype != np.bool_ else np.bool_)[0]
+        return np.pad(x, width, mode="constant", constant_values=v)
+    return np.pad(x, width, mode={"reflect": "symmetric", "replicate": "edge"}[mode])
+
+
 def gauss_chain(x, p=0.5):
     """x*p + exp(-(x^2)) with one rounding per R operator."""
     a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))

@@ -203,6 +203,43 @@ case("permute_identity", VM + ":107-108", "permute", [t_in(a24)], a24, perm=[1, 
 m34v = rmatrix(np.arange(1, 13), 3, 4)
 case("contiguous_transposed", VM + ":128-146", "permute", [t_in(m34v)], m34v.T, perm=[2, 1])
 
+# assembly and mutation (tests/testthat/test-consolidated-core.R:497-547 and
+# test-consolidated-views-memory.R:270-345).  Where a test checks only the
+# shape, the expected values follow the reference kernel's definition.
+a23 = rmatrix(np.arange(1, 7), 2, 3)
+b23 = rmatrix(np.arange(7, 13), 2, 3)
+case("concat_rbind", CC + ":497-515", "concat", [t_in(a23), t_in(b23)], np.concatenate([a23, b23], axis=0), axis=1)
+case("stack_axis3", CC + ":517-520", "stack", [t_in(a23), t_in(b23)], np.stack([a23, b23], axis=2), axis=3)
+m22 = rmatrix(np.arange(1, 5), 2, 2)
+# repeat_kernel (src/kernels/tensor_kernels.cu:381-413): out(c) = in(c %/% reps)
+case("repeat_2_1", CC + ":522-533", "repeat", [t_in(m22)], np.repeat(m22, 2, axis=0), reps=[2, 1])
+# pad_tensor(t, c(1,1,1,1)): one element of 0 on every side (R/gpuTensor.R:1816-1831)
+case("pad_1111", CC + ":535-541", "pad", [t_in(m22)], np.pad(m22, 1), pad_width=[1, 1, 1, 1])
+m45 = rmatrix(np.arange(1, 21), 4, 5)
+case("slice_row", VM + ":275-279", "subset", [t_in(m45)], m45[1, :], index=[2, None])
+case("slice_col", VM + ":281-284", "subset", [t_in(m45)], m45[:, 2], index=[None, 3])
+case("slice_block", VM + ":286-288", "subset", [t_in(m45)], m45[0:2, 1:4], index=[[1, 2], [2, 3, 4]])
+e1 = m45.copy()
+e1[1:3, 1:4] = 99
+case("assign_scalar", VM + ":293-302", "assign", [t_in(m45)], e1, index=[[2, 3], [2, 3, 4]], value=99)
+rep = rmatrix([101, 102, 103, 104, 105, 106], 2, 3)
+e2 = m45.copy()
+e2[1:3, 1:4] = rep
+case("assign_tensor", VM + ":304-311", "assign", [t_in(m45), t_in(rep)], e2, index=[[2, 3], [2, 3, 4]])
+e3 = m45.copy()
+e3[1:3, 1:4] = rmatrix([201, 202, 203, 204, 205, 206], 2, 3)
+case("assign_vector", VM + ":313-319", "assign", [t_in(m45)], e3, index=[[2, 3], [2, 3, 4]],
+     vector=[201, 202, 203, 204, 205, 206])
+v6 = np.array([1, 2, 3, 4, 5, 6.0])
+mk = np.array([True, False, True, False, True, False])
+e4 = v6.copy()
+e4[mk] = 99
+case("mask_vector", VM + ":323-334", "mask_assign", [t_in(v6)], e4, mask=mk.tolist(), value=99)
+m34m = rmatrix(np.arange(1, 13), 3, 4)
+e5 = m34m.copy()
+e5[m34m > 6] = -1
+case("mask_matrix", VM + ":336-344", "mask_assign", [t_in(m34m)], e5, mask=col(m34m > 6), value=-1)
+
 
 def main():
     out = {"generator": "tests/golden/make_golden.py",

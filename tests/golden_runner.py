@@ -48,6 +48,33 @@ def run_oracle(case):
         v = oracle.View.of(xs[0])
         perm = [p - 1 for p in args["perm"]]
         return oracle.copy(oracle.View(v.buf, [v.shape[p] for p in perm], [v.strides[p] for p in perm]))
+    if op == "concat":
+        return oracle.concat(xs, args["axis"] - 1)
+    if op == "stack":
+        return oracle.stack(xs, args["axis"] - 1)
+    if op == "repeat":
+        return oracle.repeat(xs[0], args["reps"])
+    if op == "pad":
+        pw = np.asarray(args["pad_width"]).reshape(-1, 2)
+        return oracle.pad(xs[0], pw[:, 0], pw[:, 1])
+    if op in ("subset", "assign"):
+        sl = tuple(slice(None) if i is None else (i - 1 if isinstance(i, int) else slice(i[0] - 1, i[-1]))
+                   for i in args["index"])
+        if op == "subset":
+            return xs[0][sl]
+        y = xs[0].copy()
+        if "value" in args:
+            y[sl] = args["value"]
+        elif "vector" in args:
+            y[sl] = np.asarray(args["vector"]).reshape(y[sl].shape, order="F")
+        else:
+            y[sl] = xs[1]
+        return y
+    if op == "mask_assign":
+        y = xs[0].copy()
+        m = np.asarray(args["mask"], dtype=bool).reshape(y.shape, order="F")
+        y[m] = args["value"]
+        return y
     raise KeyError(op)
 
 
@@ -79,6 +106,27 @@ def run_gpu(acd, case):
         return acd.softmax(xs[0]).as_array()
     if op == "permute":
         return acd.contiguous(acd.permute_view(xs[0], args["perm"])).as_array()
+    if op == "concat":
+        return acd.concat_tensor(xs, axis=args["axis"]).as_array()
+    if op == "stack":
+        return acd.stack_tensor(xs, axis=args["axis"]).as_array()
+    if op == "repeat":
+        return acd.repeat_tensor(xs[0], args["reps"]).as_array()
+    if op == "pad":
+        return acd.pad_tensor(xs[0], args["pad_width"]).as_array()
+    if op == "subset":
+        r = acd.subset(xs[0], *[None if i is None else i for i in args["index"]])
+        return np.asarray(r.as_array() if hasattr(r, "as_array") else r)
+    if op == "assign":
+        if "value" in args:
+            v = args["value"]
+        elif "vector" in args:
+            v = np.asarray(args["vector"], dtype=np.float64)
+        else:
+            v = xs[1]
+        return acd.assign(xs[0], *args["index"], value=v).as_array()
+    if op == "mask_assign":
+        return acd.assign(xs[0], np.asarray(args["mask"], dtype=bool), value=args["value"]).as_array()
     raise KeyError(op)
 
 
