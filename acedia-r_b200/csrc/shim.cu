@@ -430,6 +430,119 @@ void tensor_axis_argmin_float64(int64_t *idx, const double *in, const int *st, c
   axis_arg<double>(ACD_ARGMIN, idx, in, st, sh, ax, na, nd, oe, "tensor_axis_argmin_float64");
 }
 
+// ---- slice and mask assignment, concat / stack / repeat / pad ----------------
+#define ACD_SLICE_SCALAR(NAME, T, DT, BODY)                                                                  \
+  void NAME(T *data, double scalar, const int *start, const int *slice_shape, const int *strides, int ndims,  \
+            size_t total) {                                                                                   \
+    if (total == 0) return;                                                                                   \
+    acd_desc v = from_meta(data, DT, strides, slice_shape, ndims);                                            \
+    for (int k = 0; k < ndims; ++k) v.offset += (int64_t)start[k] * strides[k];                                \
+    BODY;                                                                                                     \
+  }
+ACD_SLICE_SCALAR(tensor_slice_set_scalar_float32, float, ACD_FLOAT32,
+                 shim_done(acd_fill(shim_ctx(), &v, scalar, nullptr), "tensor_slice_set_scalar_float32"))
+ACD_SLICE_SCALAR(tensor_slice_set_scalar_float64, double, ACD_FLOAT64,
+                 shim_done(acd_fill(shim_ctx(), &v, scalar, nullptr), "tensor_slice_set_scalar_float64"))
+ACD_SLICE_SCALAR(tensor_slice_add_scalar_float32, float, ACD_FLOAT32,
+                 shim_done(acd_scalar(shim_ctx(), ACD_ADD, &v, &v, scalar, nullptr),
+                           "tensor_slice_add_scalar_float32"))
+ACD_SLICE_SCALAR(tensor_slice_add_scalar_float64, double, ACD_FLOAT64,
+                 shim_done(acd_scalar(shim_ctx(), ACD_ADD, &v, &v, scalar, nullptr),
+                           "tensor_slice_add_scalar_float64"))
+#undef ACD_SLICE_SCALAR
+
+#define ACD_SLICE_TENSOR(NAME, T, DT)                                                                          \
+  void NAME(T *dest, const T *src, const int *start, const int *slice_shape, const int *dest_strides,          \
+            const int *src_strides, int ndims, size_t total) {                                                 \
+    if (total == 0) return;                                                                                     \
+    acd_desc o = from_meta(dest, DT, dest_strides, slice_shape, ndims);                                         \
+    for (int k = 0; k < ndims; ++k) o.offset += (int64_t)start[k] * dest_strides[k];                             \
+    const acd_desc x = from_meta(src, DT, src_strides, slice_shape, ndims);                                     \
+    shim_done(acd_copy(shim_ctx(), &o, &x, nullptr), #NAME);                                                    \
+  }
+ACD_SLICE_TENSOR(tensor_slice_set_tensor_float32, float, ACD_FLOAT32)
+ACD_SLICE_TENSOR(tensor_slice_set_tensor_float64, double, ACD_FLOAT64)
+#undef ACD_SLICE_TENSOR
+
+void tensor_mask_set_scalar_float32(float *data, const unsigned char *mask, float value, size_t n) {
+  if (n == 0) return;
+  const acd_desc x = flat(data, ACD_FLOAT32, n), m = flat(mask, ACD_BOOL, n);
+  shim_done(acd_mask_fill(shim_ctx(), &x, &m, value, nullptr), "tensor_mask_set_scalar_float32");
+}
+void tensor_mask_set_scalar_float64(double *data, const unsigned char *mask, double value, size_t n) {
+  if (n == 0) return;
+  const acd_desc x = flat(data, ACD_FLOAT64, n), m = flat(mask, ACD_BOOL, n);
+  shim_done(acd_mask_fill(shim_ctx(), &x, &m, value, nullptr), "tensor_mask_set_scalar_float64");
+}
+
+#define ACD_CONCAT(NAME, T, DT)                                                                                \
+  void NAME(T *result, const T **inputs, const int *input_sizes, int num, const int *result_strides,            \
+            const int *input_strides_list, const int *shape, int ndims, int axis, size_t total) {               \
+    if (total == 0) return;                                                                                     \
+    const acd_desc o = from_meta(result, DT, result_strides, shape, ndims);                                     \
+    std::vector<acd_desc> in(num);                                                                              \
+    std::vector<const acd_desc *> ptr(num);                                                                     \
+    for (int t = 0; t < num; ++t) {                                                                             \
+      std::vector<int> sh(shape, shape + ndims);                                                                \
+      sh[axis] = input_sizes[t];                                                                                \
+      in[t] = from_meta(inputs[t], DT, input_strides_list + (size_t)t * ndims, sh.data(), ndims);               \
+      ptr[t] = &in[t];                                                                                          \
+    }                                                                                                           \
+    shim_done(acd_concat(shim_ctx(), &o, ptr.data(), num, axis, nullptr), #NAME);                               \
+  }
+ACD_CONCAT(launch_concat_float32, float, ACD_FLOAT32)
+ACD_CONCAT(launch_concat_float64, double, ACD_FLOAT64)
+#undef ACD_CONCAT
+
+#define ACD_STACK(NAME, T, DT)                                                                                 \
+  void NAME(T *result, const T **inputs, int num, const int *input_strides, const int *result_shape, int ndims,  \
+            int axis, size_t total) {                                                                           \
+    if (total == 0) return;                                                                                     \
+    const acd_desc o = contiguous_of(result, DT, result_shape, ndims);                                          \
+    std::vector<int> sh;                                                                                        \
+    for (int d = 0; d < ndims; ++d)                                                                             \
+      if (d != axis) sh.push_back(result_shape[d]);                                                             \
+    std::vector<acd_desc> in(num);                                                                              \
+    std::vector<const acd_desc *> ptr(num);                                                                     \
+    for (int t = 0; t < num; ++t) {                                                                             \
+      in[t] = from_meta(inputs[t], DT, input_strides, sh.data(), ndims - 1);                                    \
+      ptr[t] = &in[t];                                                                                          \
+    }                                                                                                           \
+    shim_done(acd_stack(shim_ctx(), &o, ptr.data(), num, axis, nullptr), #NAME);                                \
+  }
+ACD_STACK(launch_stack_float32, float, ACD_FLOAT32)
+ACD_STACK(launch_stack_float64, double, ACD_FLOAT64)
+#undef ACD_STACK
+
+#define ACD_REPEAT(NAME, T, DT)                                                                                \
+  void NAME(T *result, const T *input, const int *input_strides, const int *reps, const int *input_shape,       \
+            const int *result_shape, int ndims, size_t total) {                                                 \
+    if (total == 0) return;                                                                                     \
+    const acd_desc o = contiguous_of(result, DT, result_shape, ndims);                                          \
+    const acd_desc x = from_meta(input, DT, input_strides, input_shape, ndims);                                 \
+    int64_t r[ACD_MAX_DIMS];                                                                                    \
+    for (int d = 0; d < ndims && d < ACD_MAX_DIMS; ++d) r[d] = reps[d];                                         \
+    shim_done(acd_repeat(shim_ctx(), &o, &x, r, nullptr), #NAME);                                               \
+  }
+ACD_REPEAT(launch_repeat_float32, float, ACD_FLOAT32)
+ACD_REPEAT(launch_repeat_float64, double, ACD_FLOAT64)
+#undef ACD_REPEAT
+
+#define ACD_PAD(NAME, T, DT)                                                                                   \
+  void NAME(T *result, const T *input, const int *input_strides, const int *input_shape, const int *pad_before,  \
+            const int *pad_after, const int *result_shape, int ndims, T pad_value, int pad_mode, size_t total) {   \
+    (void)pad_after;                                                                                            \
+    if (total == 0) return;                                                                                     \
+    const acd_desc o = contiguous_of(result, DT, result_shape, ndims);                                          \
+    const acd_desc x = from_meta(input, DT, input_strides, input_shape, ndims);                                 \
+    int64_t b[ACD_MAX_DIMS];                                                                                    \
+    for (int d = 0; d < ndims && d < ACD_MAX_DIMS; ++d) b[d] = pad_before[d];                                   \
+    shim_done(acd_pad(shim_ctx(), &o, &x, b, pad_mode, (double)pad_value, nullptr), #NAME);                     \
+  }
+ACD_PAD(launch_pad_float32, float, ACD_FLOAT32)
+ACD_PAD(launch_pad_float64, double, ACD_FLOAT64)
+#undef ACD_PAD
+
 void tensor_softmax_float32(float *out, const float *in, size_t n) {
   if (n == 0) return;
   const acd_desc o = flat(out, ACD_FLOAT32, n), x = flat(in, ACD_FLOAT32, n);

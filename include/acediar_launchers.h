@@ -208,6 +208,48 @@ void tensor_axis_argmin_float32(int64_t *idx, const float *in, const int *in_str
 void tensor_axis_argmin_float64(int64_t *idx, const double *in, const int *in_strides, const int *in_shape,
                                 const int *out_strides, const int *axes, int n_axes, int ndims, size_t out_elems);
 
+/* ---- slice and mask assignment (host metadata): src/kernels/tensor_slice_update.cu,
+ * called by src/TensorMutation.cpp:49-86 ---- */
+void tensor_slice_add_scalar_float32(float *data, double scalar, const int *start, const int *slice_shape,
+                                     const int *strides, int ndims, size_t total_elements);
+void tensor_slice_add_scalar_float64(double *data, double scalar, const int *start, const int *slice_shape,
+                                     const int *strides, int ndims, size_t total_elements);
+void tensor_slice_set_scalar_float32(float *data, double scalar, const int *start, const int *slice_shape,
+                                     const int *strides, int ndims, size_t total_elements);
+void tensor_slice_set_scalar_float64(double *data, double scalar, const int *start, const int *slice_shape,
+                                     const int *strides, int ndims, size_t total_elements);
+void tensor_slice_set_tensor_float32(float *dest_data, const float *src_data, const int *start,
+                                     const int *slice_shape, const int *dest_strides, const int *src_strides,
+                                     int ndims, size_t total_elements);
+void tensor_slice_set_tensor_float64(double *dest_data, const double *src_data, const int *start,
+                                     const int *slice_shape, const int *dest_strides, const int *src_strides,
+                                     int ndims, size_t total_elements);
+/* mask: one byte per element, nonzero = TRUE (C++ bool storage) */
+void tensor_mask_set_scalar_float32(float *data, const unsigned char *mask, float value, size_t total_elements);
+void tensor_mask_set_scalar_float64(double *data, const unsigned char *mask, double value, size_t total_elements);
+
+/* ---- concat / stack / repeat / pad (host metadata): src/TensorMutation.cpp:10-47 ---- */
+void launch_concat_float32(float *result, const float **inputs, const int *input_sizes, int num_tensors,
+                           const int *result_strides, const int *input_strides_list, const int *shape, int ndims,
+                           int concat_axis, size_t total_elements);
+void launch_concat_float64(double *result, const double **inputs, const int *input_sizes, int num_tensors,
+                           const int *result_strides, const int *input_strides_list, const int *shape, int ndims,
+                           int concat_axis, size_t total_elements);
+void launch_stack_float32(float *result, const float **inputs, int num_tensors, const int *input_strides,
+                          const int *result_shape, int ndims, int stack_axis, size_t total_elements);
+void launch_stack_float64(double *result, const double **inputs, int num_tensors, const int *input_strides,
+                          const int *result_shape, int ndims, int stack_axis, size_t total_elements);
+void launch_repeat_float32(float *result, const float *input, const int *input_strides, const int *repeat_counts,
+                           const int *input_shape, const int *result_shape, int ndims, size_t total_elements);
+void launch_repeat_float64(double *result, const double *input, const int *input_strides, const int *repeat_counts,
+                           const int *input_shape, const int *result_shape, int ndims, size_t total_elements);
+void launch_pad_float32(float *result, const float *input, const int *input_strides, const int *input_shape,
+                        const int *pad_before, const int *pad_after, const int *result_shape, int ndims,
+                        float pad_value, int pad_mode, size_t total_elements);
+void launch_pad_float64(double *result, const double *input, const int *input_strides, const int *input_shape,
+                        const int *pad_before, const int *pad_after, const int *result_shape, int ndims,
+                        double pad_value, int pad_mode, size_t total_elements);
+
 /* ---- softmax over the whole tensor: src/kernels/tensor_ops.cu:826-846 ---- */
 void tensor_softmax_float32(float *out, const float *in, size_t n);
 void tensor_softmax_float64(double *out, const double *in, size_t n);

@@ -93,3 +93,58 @@ def test_softmax_name_whole_tensor(lib):
     dx, out = _dev(x), torch.empty(5000, dtype=torch.float32, device="cuda")
     lib.tensor_softmax_float32(_p(out), _p(dx), ctypes.c_size_t(5000))
     assert_rel(out.cpu().numpy(), oracle.softmax(x), 1e-5, "tensor_softmax_float32")
+
+
+def test_mutation_and_assembly_names(lib):
+    """Slice/mask assignment and concat/stack/repeat/pad through the names
+    src/TensorMutation.cpp calls, host metadata as it passes them."""
+    rng = np.random.default_rng(5)
+    ints = lambda v: (ctypes.c_int * len(v))(*v)
+    m = np.arange(1, 21, dtype=np.float32).reshape(4, 5, order="F")
+    dm = _dev(m.reshape(-1, order="F"))
+    lib.tensor_slice_set_scalar_float32(_p(dm), ctypes.c_double(99.0), ints([1, 1]), ints([2, 3]), ints([1, 4]),
+                                        2, ctypes.c_size_t(6))
+    e = m.copy()
+    e[1:3, 1:4] = 99
+    lib.tensor_slice_add_scalar_float32(_p(dm), ctypes.c_double(0.5), ints([0, 0]), ints([1, 5]), ints([1, 4]),
+                                        2, ctypes.c_size_t(5))
+    e[0, :] += np.float32(0.5)
+    assert_exact(dm.cpu().numpy(), e.reshape(-1, order="F"), "slice set / add scalar")
+    src = rng.normal(size=(2, 2))
+    d64 = _dev(np.zeros(20))
+    dsrc = _dev(src.reshape(-1, order="F"))
+    lib.tensor_slice_set_tensor_float64(_p(d64), _p(dsrc), ints([2, 3]), ints([2, 2]), ints([1, 4]), ints([1, 2]),
+                                        2, ctypes.c_size_t(4))
+    z = np.zeros((4, 5))
+    z[2:4, 3:5] = src
+    assert_exact(d64.cpu().numpy(), z.reshape(-1, order="F"), "tensor_slice_set_tensor_float64")
+    mask = (rng.random(20) < 0.5).astype(np.uint8)
+    lib.tensor_mask_set_scalar_float64(_p(d64), _p(_dev(mask)), ctypes.c_double(-1.0), ctypes.c_size_t(20))
+    zz = z.reshape(-1, order="F").copy()
+    zz[mask.astype(bool)] = -1
+    assert_exact(d64.cpu().numpy(), zz, "tensor_mask_set_scalar_float64")
+
+    a = rng.normal(size=(2, 3)).astype(np.float32)
+    b = rng.normal(size=(3, 3)).astype(np.float32)
+    da, db = _dev(a.reshape(-1, order="F")), _dev(b.reshape(-1, order="F"))
+    out = torch.empty(15, dtype=torch.float32, device="cuda")
+    ptrs = (ctypes.c_void_p * 2)(da.data_ptr(), db.data_ptr())
+    lib.launch_concat_float32(_p(out), ptrs, ints([2, 3]), 2, ints([1, 5]), ints([1, 2, 1, 3]), ints([5, 3]), 2, 0,
+                              ctypes.c_size_t(15))
+    assert_exact(out.cpu().numpy(), np.concatenate([a, b], 0).reshape(-1, order="F"), "launch_concat_float32")
+    c = rng.normal(size=(2, 3)).astype(np.float32)
+    dc = _dev(c.reshape(-1, order="F"))
+    out2 = torch.empty(12, dtype=torch.float32, device="cuda")
+    ptrs = (ctypes.c_void_p * 2)(da.data_ptr(), dc.data_ptr())
+    lib.launch_stack_float32(_p(out2), ptrs, 2, ints([1, 2]), ints([2, 3, 2]), 3, 2, ctypes.c_size_t(12))
+    assert_exact(out2.cpu().numpy(), np.stack([a, c], 2).reshape(-1, order="F"), "launch_stack_float32")
+    out3 = torch.empty(24, dtype=torch.float32, device="cuda")
+    lib.launch_repeat_float32(_p(out3), _p(da), ints([1, 2]), ints([2, 2]), ints([2, 3]), ints([4, 6]), 2,
+                              ctypes.c_size_t(24))
+    assert_exact(out3.cpu().numpy(), oracle.repeat(a, (2, 2)).reshape(-1, order="F"), "launch_repeat_float32")
+    out4 = torch.empty(4 * 7, dtype=torch.float32, device="cuda")
+    for mode, name in [(0, "constant"), (1, "reflect"), (2, "replicate")]:
+        lib.launch_pad_float32(_p(out4), _p(da), ints([1, 2]), ints([2, 3]), ints([1, 2]), ints([1, 2]),
+                               ints([4, 7]), 2, ctypes.c_float(3.0), mode, ctypes.c_size_t(28))
+        assert_exact(out4.cpu().numpy(), oracle.pad(a, [1, 2], [1, 2], name, 3.0).reshape(-1, order="F"),
+                     "launch_pad_float32 " + name)
