@@ -10,4 +10,5 @@ from .tensor import (  # noqa: F401
     log, max, mean, min, permute_view, pmax, pmin, prod, relu, reshape, round, shape, sigmoid, sin, softmax, sqrt,
     sum, sum_var, synchronize, tanh, tensor_count, tensor_max, tensor_mean, tensor_min, tensor_prod, tensor_sum,
     tensor_var, to_dtype, transpose, transpose_view, var, view, which_max, which_min, subset, assign, concat,
-    concat_tensor, stack, stack_tensor, repeat_tensor, pad, pad_tensor)
+    concat_tensor, stack, stack_tensor, repeat_tensor, pad, pad_tensor, set_seed, rand_tensor, rnorm_tensor,
+    rand_tensor_uniform, rand_tensor_normal, runif, rnorm)

@@ -93,6 +93,7 @@ def _bind(lib):
         "acd_stack": ([vp, dp, ctypes.POINTER(dp), i32, i32, vp], i32),
         "acd_repeat": ([vp, dp, dp, P(i64), vp], i32),
         "acd_pad": ([vp, dp, dp, P(i64), i32, ctypes.c_double, vp], i32),
+        "acd_rand": ([vp, dp, i32, ctypes.c_double, ctypes.c_double, ctypes.c_uint64, ctypes.c_uint64, vp], i32),
         "acd_reduce": ([vp, i32, dp, dp, u32, vp], i32),
         "acd_sum_var": ([vp, dp, dp, dp, vp], i32),
         "acd_arg_reduce": ([vp, i32, dp, dp, dp, i32, i32, vp], i32),

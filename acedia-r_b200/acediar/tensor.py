@@ -17,6 +17,7 @@ Reference semantics kept on purpose:
 import builtins
 import ctypes
 import numbers
+import os
 
 import numpy as np
 import torch
@@ -493,6 +494,72 @@ def pad_tensor(x, pad_width, mode="constant", value=0):
 
 concat = concat_tensor
 stack = stack_tensor
+
+
+# ---- random tensors (src/TensorRandom.cpp, R/gpuTensor.R:2342-2524) ---------
+# A counter-based stream: (seed, position).  Every call takes the next n
+# positions (rounded up to a multiple of 4).  set_seed makes runs repeatable;
+# the initial seed comes from the OS, as the reference seeds from the clock.
+_rng = {"seed": int.from_bytes(os.urandom(8), "little"), "pos": 0}
+
+
+def set_seed(seed):
+    """Seeds the tensor random stream (position 0 of seed `seed`)."""
+    _rng["seed"] = int(seed) & (2 ** 64 - 1)
+    _rng["pos"] = 0
+
+
+def _rand(shape, dtype, dist, a, b):
+    shape = tuple(int(s) for s in (shape if not isinstance(shape, numbers.Number) else [shape]))
+    if any(s <= 0 for s in shape):
+        raise ValueError("All shape dimensions must be positive")
+    dt = _ALIASES.get(dtype, dtype)
+    if dt not in ("float", "double"):
+        raise ValueError("Unsupported dtype for random tensor. Use 'float' or 'double'")
+    out = _alloc(shape, dt)
+    pos = _rng["pos"]
+    _rng["pos"] = pos + (out.size + 3) // 4 * 4
+    L.check(L.lib().acd_rand(context(), ctypes.byref(out.desc()), dist, ctypes.c_double(a), ctypes.c_double(b),
+                             ctypes.c_uint64(_rng["seed"]), ctypes.c_uint64(pos), _stream()), "rand_tensor")
+    return out
+
+
+def rand_tensor(shape, dtype="float"):
+    """rand_tensor (src/TensorRandom.cpp:42-110): uniform on [0, 1)."""
+    return _rand(shape, dtype, 0, 0.0, 1.0)
+
+
+def rnorm_tensor(shape, mean=0.0, sd=1.0, dtype="float"):
+    """rnorm_tensor (src/TensorRandom.cpp:120-224): normal(mean, sd)."""
+    return _rand(shape, dtype, 1, float(mean), float(sd))
+
+
+def rand_tensor_uniform(shape, dtype="float", min=0.0, max=1.0):
+    """rand_tensor_uniform (R/gpuTensor.R): uniform on [min, max)."""
+    if not (min < max):
+        raise ValueError("min must be less than max")
+    return _rand(shape, dtype, 0, float(min), float(max))
+
+
+def rand_tensor_normal(shape, mean=0.0, sd=1.0, dtype="float"):
+    """rand_tensor_normal (R/gpuTensor.R): normal(mean, sd)."""
+    if not sd > 0:
+        raise ValueError("sd must be positive")
+    return _rand(shape, dtype, 1, float(mean), float(sd))
+
+
+def runif(x, min=0.0, max=1.0):
+    """runif.gpuTensor: a new tensor of x's shape and dtype, uniform on [min, max)."""
+    if not isinstance(x, gpuTensor):
+        raise ValueError("runif method requires a gpuTensor object or numeric count")
+    return rand_tensor_uniform(x.shape, x.dtype, min, max)
+
+
+def rnorm(x, mean=0.0, sd=1.0):
+    """rnorm.gpuTensor: a new tensor of x's shape and dtype, normal(mean, sd)."""
+    if not isinstance(x, gpuTensor):
+        raise ValueError("rnorm method requires a gpuTensor object or numeric count")
+    return rand_tensor_normal(x.shape, mean, sd, x.dtype)
 
 
 _DTYPE_ALIASES = {"float32": "float", "float": "float", "float64": "double", "double": "double",

@@ -200,6 +200,16 @@ acd_status acd_repeat(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, con
 acd_status acd_pad(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, const int64_t *before, int32_t mode,
                    double value, acd_stream stream);
 
+/* ---- random tensors --------------------------------------------------- */
+/* Fills a contiguous float32/float64 view: dist 0 = uniform on [a, b),
+ * dist 1 = normal with mean a and sd b.  Element i takes counter position
+ * offset + i of Philox4x32-10 keyed by `seed`, so a shard generated with
+ * offset = its first global index holds exactly the values of the whole
+ * tensor.  Replaces rand_tensor / rnorm_tensor (src/TensorRandom.cpp:42-224),
+ * which draw from cuRAND seeded with time(NULL). */
+acd_status acd_rand(acd_ctx *ctx, const acd_desc *out, int32_t dist, double a, double b, uint64_t seed,
+                    uint64_t offset, acd_stream stream);
+
 /* dtype conversion, out = as.<dtype>(in) over any two views of one shape.
  * Replaces tensor_to_dtype_unified (src/TensorDataAccess.cpp:152-190), whose
  * kernel is type_conversion_kernel (src/kernels/tensor_kernels.cu:52-57,

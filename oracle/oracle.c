@@ -293,6 +293,69 @@ void orc_convert(int from, int to, const void *in, int nd, const int64_t *shape,
   for (int64_t i = 0; i < n; ++i) convert_one(from, to, in, offset_of(i, nd, shape, st), out, i);
 }
 
+/* ---- counter-based random tensors --------------------------------------
+ * Philox4x32-10 (Salmon, Moraes, Dror and Shaw, SC 2011) keyed by the 64-bit
+ * seed; element i takes counter position offset + i.  Restates the
+ * generator of this library (the reference draws from cuRAND seeded with
+ * time(NULL), src/TensorRandom.cpp:19-27, which no run can reproduce).
+ * Uniforms use the same float64 arithmetic as the device; normals are
+ * evaluated in long double and rounded once (the device uses float32 or
+ * float64 math, so the tests compare normals within a tolerance). */
+static void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
+  for (int r = 0; r < 10; ++r) {
+    const uint64_t p0 = (uint64_t)0xD2511F53u * c[0], p1 = (uint64_t)0xCD9E8D57u * c[2];
+    const uint32_t n0 = (uint32_t)(p1 >> 32) ^ c[1] ^ k0, n1 = (uint32_t)p1;
+    const uint32_t n2 = (uint32_t)(p0 >> 32) ^ c[3] ^ k1, n3 = (uint32_t)p0;
+    c[0] = n0;
+    c[1] = n1;
+    c[2] = n2;
+    c[3] = n3;
+    k0 += 0x9E3779B9u;
+    k1 += 0xBB67AE85u;
+  }
+}
+
+/* one raw Philox4x32-10 block, for the known-answer tests */
+void orc_philox(const uint32_t ctr[4], const uint32_t key[2], uint32_t out[4]) {
+  for (int k = 0; k < 4; ++k) out[k] = ctr[k];
+  philox4x32_10(out, key[0], key[1]);
+}
+
+void orc_rand(int dt, int dist, double a, double b, uint64_t seed, uint64_t offset, int64_t n, void *out) {
+  const int pb = dt == DT_F32 ? 4 : 2;
+  const uint32_t k0 = (uint32_t)seed, k1 = (uint32_t)(seed >> 32);
+  const long double two_pi = 6.283185307179586476925286766559005768L;
+  for (int64_t i = 0; i < n; ++i) {
+    const uint64_t pos = offset + (uint64_t)i, g = pos / (uint64_t)pb;
+    const int j = (int)(pos % (uint64_t)pb);
+    uint32_t w[4] = {(uint32_t)g, (uint32_t)(g >> 32), 0u, 0u};
+    philox4x32_10(w, k0, k1);
+    if (dt == DT_F32) {
+      if (dist == 0) {
+        const float u = (float)(w[j] >> 8) * 0x1p-24f;
+        ((float *)out)[i] = (float)(a + (b - a) * (double)u);
+      } else {
+        const int p = j / 2;
+        const long double u = (long double)((w[2 * p] >> 8) + 1u) * 0x1p-24L;
+        const long double t = (long double)(w[2 * p + 1] >> 8) * 0x1p-24L;
+        const long double r = sqrtl(-2.0L * logl(u));
+        const long double z = (j % 2 == 0) ? r * cosl(two_pi * t) : r * sinl(two_pi * t);
+        ((float *)out)[i] = (float)(a + b * (double)(float)z);
+      }
+    } else {
+      const uint64_t x0 = (((uint64_t)w[0] << 32) | w[1]) >> 11, x1 = (((uint64_t)w[2] << 32) | w[3]) >> 11;
+      if (dist == 0) {
+        ((double *)out)[i] = a + (b - a) * ((double)(j == 0 ? x0 : x1) * 0x1p-53);
+      } else {
+        const long double u = (long double)(x0 + 1) * 0x1p-53L, t = (long double)x1 * 0x1p-53L;
+        const long double r = sqrtl(-2.0L * logl(u));
+        const double z = (double)(j == 0 ? r * cosl(two_pi * t) : r * sinl(two_pi * t));
+        ((double *)out)[i] = a + b * z;
+      }
+    }
+  }
+}
+
 /* ---- reductions over a set of reduced values ---------------------------- */
 static long double r_mean(const long double *v, int64_t n) {
   long double s = 0.0L;

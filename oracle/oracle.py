@@ -178,6 +178,17 @@ def convert(x, to_dtype):
     return _result(out, v.shape)
 
 
+def rand(n, dtype, dist, a, b, seed, offset=0):
+    """Counter-based random values (Philox4x32-10): dist "uniform" on [a, b)
+    or "normal" with mean a and sd b; element i uses counter offset + i."""
+    dt = np.dtype(dtype)
+    out = np.empty(int(n), dtype=dt)
+    lib().orc_rand(DT[dt], 0 if dist == "uniform" else 1, ctypes.c_double(a), ctypes.c_double(b),
+                   ctypes.c_uint64(seed), ctypes.c_uint64(offset), ctypes.c_int64(int(n)),
+                   out.ctypes.data_as(ctypes.c_void_p))
+    return out
+
+
 # ---- assembly (pure data movement, restated with numpy on logical arrays) ----
 def concat(arrays, axis):
     """concat_kernel (src/kernels/tensor_kernels.cu:298-341): the inputs in
