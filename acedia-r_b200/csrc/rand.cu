@@ -16,8 +16,9 @@
 //   float64 normal   2 values: Box-Muller on 53-bit uniforms from (w0, w1), (w2, w3)
 // Box-Muller: r = sqrt(-2 log u), (z0, z1) = r (cos 2 pi v, sin 2 pi v) with u
 // in (0, 1] (a uniform shifted by one step) and v in [0, 1).  Uniforms are
-// scaled as min + (max - min) u and normals as mean + sd z, both in float64
-// and rounded once to the tensor dtype.
+// scaled as min + (max - min) u and normals as mean + sd z: one fused
+// multiply-add in the tensor dtype (float32: with min, max - min, mean and sd
+// rounded to float32 first).
 #include "common.cuh"
 
 namespace acd {
@@ -50,9 +51,11 @@ __device__ __forceinline__ void block_values(uint64_t g, uint32_t k0, uint32_t k
   philox4x32_10(w, k0, k1);
   if constexpr (std::is_same<T, float>::value) {
     if constexpr (DIST == 0) {
+      const float span = (float)(b - a), lo = (float)a;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) v[j] = (float)(a + (b - a) * (double)((float)(w[j] >> 8) * 0x1p-24f));
+      for (int j = 0; j < 4; ++j) v[j] = fmaf(span, (float)(w[j] >> 8) * 0x1p-24f, lo);
     } else {
+      const float sd = (float)b, mu = (float)a;
 #pragma unroll
       for (int p = 0; p < 2; ++p) {
         const float u = (float)((w[2 * p] >> 8) + 1u) * 0x1p-24f;  // (0, 1]
@@ -60,24 +63,24 @@ __device__ __forceinline__ void block_values(uint64_t g, uint32_t k0, uint32_t k
         const float r = sqrtf(-2.0f * logf(u));
         float sn, cs;
         sincospif(2.0f * t, &sn, &cs);
-        v[2 * p] = (float)(a + b * (double)(r * cs));
-        v[2 * p + 1] = (float)(a + b * (double)(r * sn));
+        v[2 * p] = fmaf(sd, r * cs, mu);
+        v[2 * p + 1] = fmaf(sd, r * sn, mu);
       }
     }
   } else {
     const uint64_t x0 = (((uint64_t)w[0] << 32) | w[1]) >> 11;
     const uint64_t x1 = (((uint64_t)w[2] << 32) | w[3]) >> 11;
     if constexpr (DIST == 0) {
-      v[0] = a + (b - a) * ((double)x0 * 0x1p-53);
-      v[1] = a + (b - a) * ((double)x1 * 0x1p-53);
+      v[0] = fma(b - a, (double)x0 * 0x1p-53, a);
+      v[1] = fma(b - a, (double)x1 * 0x1p-53, a);
     } else {
       const double u = (double)(x0 + 1) * 0x1p-53;  // (0, 1]
       const double t = (double)x1 * 0x1p-53;        // [0, 1)
       const double r = sqrt(-2.0 * log(u));
       double sn, cs;
       sincospi(2.0 * t, &sn, &cs);
-      v[0] = a + b * (r * cs);
-      v[1] = a + b * (r * sn);
+      v[0] = fma(b, r * cs, a);
+      v[1] = fma(b, r * sn, a);
     }
   }
 }

@@ -27,7 +27,7 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 sys.path.insert(0, os.path.join(ROOT, "acedia-r_b200"))
 
 N0, N1, N2 = 256, 512, 32768
-CHUNK = 128  # slices along axis 3 generated per seed (independent of the GPU count)
+CHUNK = 128  # shards hold whole multiples of 128 slices along axis 3
 SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
 BYTES_PER_ELEM = {"transpose": 8, "fused_chain": 8, "stats": 4, "argmax_keys": 4}
@@ -149,7 +149,7 @@ def reference_arm(a):
         "metric": "Gelem/s, strided-views step (permute->contiguous, x*0.5+exp(-x^2), sum/var, argmax axis 1)",
         "value": round(v, 4), "unit": "Gelem/s", "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
         "ms_per_step": round(dt * 1e3, 3), "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
-        "dtype": "f32", "data": "synthetic N(0,1), seed 42",
+        "dtype": "f32", "data": "synthetic N(0,1), numpy PCG64 seed 42 (the CPU sample; the GPU arm uses acd_rand)",
         "config": {"workload": "strided views 256x512x32768 f32 (CPU sample 256x512x%d)" % n2,
                    "l2": "inputs larger than L2"},
         "impl": "reference",
@@ -322,6 +322,9 @@ def run_config_report(a):
         ops.append(_op("sum+var fused", lambda: acd.sum_var(T), B, peak, note="includes two 8-byte D2H reads"))
         ops.append(_op("which.max(T)", lambda: Tm._arg("argmax", T), B, peak))
         ops.append(_op("as.double(T)", lambda: acd.to_dtype(T, "double"), B + 2 * B, peak, graph=True))
+        ops.append(_op("rnorm_tensor(4096x4096x16)", lambda: acd.rnorm_tensor(shp), B, peak, graph=True,
+                       note="Philox4x32-10 + Box-Muller, write-only"))
+        ops.append(_op("rand_tensor(4096x4096x16)", lambda: acd.rand_tensor(shp), B, peak, graph=True))
         ops.append(_op("as.integer(T)", lambda: acd.to_dtype(T, "int32"), 2 * B, peak, graph=True))
         for ax in (1, 2, 3):
             kept = n // shp[ax - 1]
@@ -388,13 +391,13 @@ def main():
     nloc = N0 * N1 * n2l
     ntot = N0 * N1 * n2
 
-    # ---- input: x[:, :, lo:hi], generated chunk by chunk (seed = SEED + chunk index)
+    # ---- input: x[:, :, lo:hi] from this library's counter-based generator:
+    # element (a, b, c) is counter position a + 256 (b + 512 c) of seed 42, so
+    # every GPU count holds exactly the same tensor
     x = _alloc((N0, N1, n2l), "float", dev)
-    g = torch.Generator(device=dev)
-    per = N0 * N1 * CHUNK
-    for c in range(n2l // CHUNK):
-        g.manual_seed(SEED + (lo // CHUNK) + c)
-        x.storage[c * per:(c + 1) * per].normal_(generator=g)
+    L.check(lib.acd_rand(ctx, ctypes.byref(x.desc()), 1, ctypes.c_double(0.0), ctypes.c_double(1.0),
+                         ctypes.c_uint64(SEED), ctypes.c_uint64(lo * N0 * N1),
+                         ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)), "rand")
 
     # ---- preallocated outputs
     xp_view = acediar.permute_view(x, [3, 1, 2])
@@ -563,8 +566,8 @@ def main():
             "metric": "Gelem/s, strided-views step (permute->contiguous, x*0.5+exp(-x^2), sum/var, argmax axis 1)",
             "value": round(value, 4), "unit": "Gelem/s", "n_gpus": world, "steps": a.steps,
             "warmup": max(3, a.warmup), "ms_per_step": round(ms_max, 4), "higher_is_better": True,
-            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1), Philox seed 42 per "
-            "128-slice chunk (identical for any GPU count)",
+            "scaling": "strong", "vs_baseline": None, "dtype": "f32", "data": "synthetic N(0,1) from acd_rand (Philox4x32-10, seed 42, counter = "
+            "global element index: identical for any GPU count)",
             "config": {"workload": "strided views 256x512x%d f32, sharded on axis 3" % n2,
                        "l2": "inputs larger than L2 (16 GiB), no flush needed",
                        "parallelism": "shard%d" % world, "elements": ntot},

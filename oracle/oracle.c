@@ -298,7 +298,8 @@ void orc_convert(int from, int to, const void *in, int nd, const int64_t *shape,
  * seed; element i takes counter position offset + i.  Restates the
  * generator of this library (the reference draws from cuRAND seeded with
  * time(NULL), src/TensorRandom.cpp:19-27, which no run can reproduce).
- * Uniforms use the same float64 arithmetic as the device; normals are
+ * Uniforms use the same arithmetic as the device (one fused multiply-add in
+ * the tensor dtype, C99 fma/fmaf being correctly rounded); normals are
  * evaluated in long double and rounded once (the device uses float32 or
  * float64 math, so the tests compare normals within a tolerance). */
 static void philox4x32_10(uint32_t c[4], uint32_t k0, uint32_t k1) {
@@ -333,24 +334,24 @@ void orc_rand(int dt, int dist, double a, double b, uint64_t seed, uint64_t offs
     if (dt == DT_F32) {
       if (dist == 0) {
         const float u = (float)(w[j] >> 8) * 0x1p-24f;
-        ((float *)out)[i] = (float)(a + (b - a) * (double)u);
+        ((float *)out)[i] = fmaf((float)(b - a), u, (float)a);
       } else {
         const int p = j / 2;
         const long double u = (long double)((w[2 * p] >> 8) + 1u) * 0x1p-24L;
         const long double t = (long double)(w[2 * p + 1] >> 8) * 0x1p-24L;
         const long double r = sqrtl(-2.0L * logl(u));
         const long double z = (j % 2 == 0) ? r * cosl(two_pi * t) : r * sinl(two_pi * t);
-        ((float *)out)[i] = (float)(a + b * (double)(float)z);
+        ((float *)out)[i] = fmaf((float)b, (float)z, (float)a);
       }
     } else {
       const uint64_t x0 = (((uint64_t)w[0] << 32) | w[1]) >> 11, x1 = (((uint64_t)w[2] << 32) | w[3]) >> 11;
       if (dist == 0) {
-        ((double *)out)[i] = a + (b - a) * ((double)(j == 0 ? x0 : x1) * 0x1p-53);
+        ((double *)out)[i] = fma(b - a, (double)(j == 0 ? x0 : x1) * 0x1p-53, a);
       } else {
         const long double u = (long double)(x0 + 1) * 0x1p-53L, t = (long double)x1 * 0x1p-53L;
         const long double r = sqrtl(-2.0L * logl(u));
         const double z = (double)(j == 0 ? r * cosl(two_pi * t) : r * sinl(two_pi * t));
-        ((double *)out)[i] = a + b * z;
+        ((double *)out)[i] = fma(b, z, a);
       }
     }
   }
