@@ -23,7 +23,7 @@ UNARY = {n: i for i, n in enumerate(
 BINARY = {n: i for i, n in enumerate(
     ["add", "sub", "mul", "div", "max", "min", "pow", "gt", "lt", "eq", "ne", "ge", "le", "rsub", "rdiv"])}
 FUSED = {"scale_add_exp_neg_square": 0, "add_relu": 1, "tanh_scale": 2}
-REDUCE = {n: i for i, n in enumerate(["sum", "mean", "max", "min", "prod", "var", "count"])}
+REDUCE = {n: i for i, n in enumerate(["sum", "mean", "max", "min", "prod", "var", "count", "any", "all"])}
 ARG = {"argmax": 0, "argmin": 1}
 SCAN = {"cumsum": 0, "cumprod": 1}
 

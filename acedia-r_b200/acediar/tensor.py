@@ -338,13 +338,13 @@ def _ranges(x, idx, what):
             starts.append(0), counts.append(n), keep.append(True)
             continue
         v = [int(i)] if isinstance(i, numbers.Number) else [int(k) for k in i]
-        if any(k <= 0 for k in v):
+        if builtins.any(k <= 0 for k in v):
             raise ValueError("Only positive indices are supported in this implementation" if what == "[" else
                              "Negative or zero indices not supported in slice assignment")
-        if any(k > n for k in v):
+        if builtins.any(k > n for k in v):
             raise ValueError("Index %d is out of bounds for dimension %d with size %d" % (builtins.max(v), d + 1, n)
                              if what == "[" else "Index out of bounds in slice assignment")
-        if any(b - a != 1 for a, b in zip(v, v[1:])):
+        if builtins.any(b - a != 1 for a, b in zip(v, v[1:])):
             raise ValueError("Only contiguous ranges are supported in this basic implementation" if what == "[" else
                              "Only contiguous ranges supported in slice assignment")
         starts.append(v[0] - 1), counts.append(len(v)), keep.append(len(v) > 1 or not isinstance(i, numbers.Number))
@@ -424,7 +424,7 @@ def concat_tensor(lst, axis=1):
     if a < 0 or a >= base.ndims:
         raise ValueError("axis out of range")
     shape = list(base.shape)
-    shape[a] = builtins.sum(t.shape[a] for t in lst) if all(t.ndims == base.ndims for t in lst) else -1
+    shape[a] = builtins.sum(t.shape[a] for t in lst) if builtins.all(t.ndims == base.ndims for t in lst) else -1
     if shape[a] < 0:
         raise ValueError("All tensors must have same number of dims")
     out = _alloc(tuple(shape), base.dtype, base.device)
@@ -456,7 +456,7 @@ def repeat_tensor(x, reps):
     reps = [int(r) for r in (reps if not isinstance(reps, numbers.Number) else [reps])]
     if len(reps) != x.ndims:
         raise ValueError("repeats length must match tensor dims")
-    if any(r <= 0 for r in reps):
+    if builtins.any(r <= 0 for r in reps):
         raise ValueError("repeat counts must be positive")
     out = _alloc(tuple(s * r for s, r in zip(x.shape, reps)), x.dtype, x.device)
     rp = (ctypes.c_int64 * len(reps))(*reps)
@@ -511,7 +511,7 @@ def set_seed(seed):
 
 def _rand(shape, dtype, dist, a, b):
     shape = tuple(int(s) for s in (shape if not isinstance(shape, numbers.Number) else [shape]))
-    if any(s <= 0 for s in shape):
+    if builtins.any(s <= 0 for s in shape):
         raise ValueError("All shape dimensions must be positive")
     dt = _ALIASES.get(dtype, dtype)
     if dt not in ("float", "double"):
@@ -642,6 +642,27 @@ def tensor_min(x, axis=None, keep_dims=False): return _reduce("min", x, axis, ke
 def tensor_prod(x, axis=None, keep_dims=False): return _reduce("prod", x, axis, keep_dims)
 def tensor_var(x, axis=None, keep_dims=False): return _reduce("var", x, axis, keep_dims)
 def tensor_count(x, axis=None, keep_dims=False): return _reduce("count", x, axis, keep_dims)
+
+
+def _logical(op, x, axis):
+    r = _reduce(op, x, axis, False, out_dtype="int32")
+    if axis is not None:
+        return r
+    v = int(r.as_array().reshape(-1)[0])
+    return None if v == np.iinfo(np.int32).min else bool(v)
+
+
+def any(x, axis=None):
+    """any.gpuTensor (R/gpuTensor.R:2178-2187), on the device: TRUE if an
+    element is non-zero, else NA (None) if an element is NaN, else FALSE.
+    With `axis`, an int32 tensor of 1 / 0 / NA (INT32_MIN)."""
+    return _logical("any", x, axis)
+
+
+def all(x, axis=None):
+    """all.gpuTensor (R/gpuTensor.R:2197-2206), on the device: FALSE if an
+    element is zero, else NA (None) if an element is NaN, else TRUE."""
+    return _logical("all", x, axis)
 
 
 def _r_reduce(op):

@@ -653,6 +653,8 @@ static acd_status reduce_t(acd_ctx *ctx, int op, const Plan &p, const OutSpec &o
     case ACD_RED_MAX: return run_plan<ExtAcc<T, true>, T>(ctx, p, os, s);
     case ACD_RED_MIN: return run_plan<ExtAcc<T, false>, T>(ctx, p, os, s);
     case ACD_RED_COUNT: return run_plan<CountAcc<T>, T>(ctx, p, os, s);
+    case ACD_RED_ANY: return run_plan<TruthAcc<T, false>, T>(ctx, p, os, s);
+    case ACD_RED_ALL: return run_plan<TruthAcc<T, true>, T>(ctx, p, os, s);
     case ACD_RED_PROD:
       if constexpr (fl) return run_plan<ProdAcc<T>, T>(ctx, p, os, s);
       break;
@@ -722,7 +724,7 @@ acd_status acd_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
   if (!ctx) return fail(ACD_ERR_INVALID, "acd_reduce: null context");
   ACD_TRY(check_desc(out, "out"));
   ACD_TRY(check_desc(in, "in"));
-  if (op < ACD_RED_SUM || op > ACD_RED_COUNT) return fail(ACD_ERR_INVALID, "acd_reduce: bad op %d", op);
+  if (op < ACD_RED_SUM || op > ACD_RED_ALL) return fail(ACD_ERR_INVALID, "acd_reduce: bad op %d", op);
   if (in->ndim < 32 && (axes_mask >> in->ndim) != 0u) return fail(ACD_ERR_AXIS, "acd_reduce: axis outside the tensor");
   if (in->ndim == 0) axes_mask = 0;
   ACD_TRY(check_out_count(out, kept_count(in, axes_mask), "acd_reduce"));

@@ -139,6 +139,38 @@ struct CountAcc {
   __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const { store_i(os.out, os.dt, oi, c); }
 };
 
+// any / all: which truth values occur (bit 1 TRUE = non-zero, bit 2 FALSE,
+// bit 4 NA = NaN or an NA integer); the result follows R's three-valued
+// logic (an empty reduction: any FALSE, all TRUE).
+template <typename T, bool ALL>
+struct TruthAcc {
+  static constexpr bool kShift = false;
+  uint32_t f;
+  __device__ __forceinline__ void init() { f = 0u; }
+  __device__ __forceinline__ void set_shift(T) {}
+  __device__ __forceinline__ void add(T x, int64_t) {
+    bool is_na;
+    if constexpr (std::is_floating_point<T>::value)
+      is_na = x != x;
+    else if constexpr (std::is_same<T, int32_t>::value)
+      is_na = x == INT32_MIN;
+    else if constexpr (std::is_same<T, int64_t>::value)
+      is_na = x == INT64_MIN;
+    else
+      is_na = false;
+    f |= is_na ? 4u : (x != T(0) ? 1u : 2u);
+  }
+  __device__ __forceinline__ void merge(const TruthAcc &o) { f |= o.f; }
+  __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const {
+    long long r;
+    if (ALL)
+      r = (f & 2u) ? 0 : ((f & 4u) ? (long long)INT32_MIN : 1);
+    else
+      r = (f & 1u) ? 1 : ((f & 4u) ? (long long)INT32_MIN : 0);
+    store_i(os.out, os.dt, oi, r);
+  }
+};
+
 // Nonzero bytes of a 32-bit word: each byte's bits are folded into its bit 0
 // (the shifts stay inside the byte for bits 0..3, which are all that is
 // kept), then the marks are counted.

@@ -110,7 +110,15 @@ typedef enum {
 typedef enum {
   ACD_RED_SUM = 0, ACD_RED_MEAN = 1, ACD_RED_MAX = 2, ACD_RED_MIN = 3,
   ACD_RED_PROD = 4, ACD_RED_VAR = 5, /* sample variance, divisor n-1 */
-  ACD_RED_COUNT = 6                  /* number of non-zero elements */
+  ACD_RED_COUNT = 6,                 /* number of non-zero elements */
+  /* any / all with R's logical rules: an element is TRUE when non-zero,
+   * NA when NaN (or an NA integer, INT_MIN); any = TRUE if some element is
+   * TRUE, else NA if some is NA, else FALSE; all = FALSE if some element is
+   * FALSE, else NA if some is NA, else TRUE.  Written as 1 / 0 / NA
+   * (INT32_MIN, R's NA_LOGICAL) to an int32 output.  The reference converts
+   * the tensor on the host (any.gpuTensor / all.gpuTensor,
+   * R/gpuTensor.R:2178-2206). */
+  ACD_RED_ANY = 7, ACD_RED_ALL = 8
 } acd_reduce_op;
 
 typedef enum { ACD_ARGMAX = 0, ACD_ARGMIN = 1 } acd_arg_op;

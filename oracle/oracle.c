@@ -46,7 +46,7 @@ enum {
 enum {
   B_ADD = 0, B_SUB, B_MUL, B_DIV, B_MAX, B_MIN, B_POW, B_GT, B_LT, B_EQ, B_NE, B_GE, B_LE, B_RSUB, B_RDIV
 };
-enum { R_SUM = 0, R_MEAN, R_MAX, R_MIN, R_PROD, R_VAR, R_COUNT };
+enum { R_SUM = 0, R_MEAN, R_MAX, R_MIN, R_PROD, R_VAR, R_COUNT, R_ANY, R_ALL };
 
 static long double ld_get(const void *p, int dt, int64_t i) {
   switch (dt) {
@@ -438,6 +438,22 @@ int orc_reduce(int op, int dt, const void *in, int nd, const int64_t *shape, con
   for (int64_t o = 0; o < O; ++o) {
     const int64_t base = offset_of(o, nk, ks, kst);
     for (int64_t j = 0; j < R; ++j) v[j] = ld_get(in, dt, base + offset_of(j, nr, rs, rst));
+    if (op == R_ANY || op == R_ALL) {
+      /* R's any()/all() over as.logical(x): NaN and NA integers are NA; the
+       * result is 1, 0 or NA (returned as NaN) */
+      int64_t t = 0, na = 0;
+      for (int64_t j = 0; j < R; ++j) {
+        const int is_na = isnan(v[j]) || (dt == DT_I32 && v[j] == (long double)INT32_MIN) ||
+                          (dt == DT_I64 && v[j] == (long double)INT64_MIN);
+        na += is_na;
+        t += !is_na && v[j] != 0.0L;
+      }
+      if (op == R_ANY)
+        out[o] = t > 0 ? 1.0 : (na > 0 ? NAN : 0.0);
+      else
+        out[o] = (t + na < R) ? 0.0 : (na > 0 ? NAN : 1.0);
+      continue;
+    }
     out[o] = (double)reduce_vals(op, v, R);
   }
   free(v);

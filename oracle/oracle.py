@@ -29,7 +29,7 @@ UNARY = {n: i for i, n in enumerate(
      "neg", "square", "copy"])}
 BINARY = {n: i for i, n in enumerate(
     ["add", "sub", "mul", "div", "max", "min", "pow", "gt", "lt", "eq", "ne", "ge", "le", "rsub", "rdiv"])}
-REDUCE = {n: i for i, n in enumerate(["sum", "mean", "max", "min", "prod", "var", "count"])}
+REDUCE = {n: i for i, n in enumerate(["sum", "mean", "max", "min", "prod", "var", "count", "any", "all"])}
 COMPARE = {"gt", "lt", "eq", "ne", "ge", "le"}
 
 _i64p = ctypes.POINTER(ctypes.c_int64)

@@ -240,6 +240,30 @@ e5 = m34m.copy()
 e5[m34m > 6] = -1
 case("mask_matrix", VM + ":336-344", "mask_assign", [t_in(m34m)], e5, mask=col(m34m > 6), value=-1)
 
+# any / all (tests/testthat/test-logical-reductions.R): R's any(x != 0) / all(x != 0)
+LR = "tests/testthat/test-logical-reductions.R"
+for cid, lines, op, data, dtype in [
+        ("any_1d_true", "25-39", "any", [0, 0, 1, 0], "float"), ("any_1d_false", "40-47", "any", [0, 0, 0, 0], "float"),
+        ("any_1d_ones", "48-53", "any", [1, 1, 1, 1], "float"), ("any_f32_half", "55-64", "any", [0, 0, 0.5, 0], "float"),
+        ("any_f64_zero", "66-72", "any", [0, 0, 0, 0], "double"), ("any_negative", "118-121", "any", [0, -1, 0, 0], "float"),
+        ("any_small", "123-126", "any", [0, 0, 1e-10, 0], "float"),
+        ("all_1d_true", "144-152", "all", [1, 2, 3, 4], "float"), ("all_1d_some_zero", "154-159", "all", [1, 0, 3, 4], "float"),
+        ("all_1d_zeros", "161-166", "all", [0, 0, 0, 0], "float"), ("all_f32", "174-180", "all", [1.5, 2.7, 0.1, 3.9], "float"),
+        ("all_f64_zero", "182-187", "all", [1.5, 0, 2.7, 3.9], "double"), ("all_negative", "248-251", "all", [-1, -2, -3, -4], "float"),
+        ("all_mixed_zero", "253-256", "all", [-1, 2, 0, -4], "float"), ("all_small", "258-261", "all", [1e-10, 2e-10, 3e-10, 4e-10], "float")]:
+    d = np.asarray(data, dtype=np.float64)
+    case(cid, LR + ":" + lines, op, [t_in(d, dtype)], np.float64((d != 0).any() if op == "any" else (d != 0).all()))
+mz = rmatrix([0, 0, 1, 0, 0, 0], 2, 3)
+case("any_2d", LR + ":75-83", "any", [t_in(mz)], np.float64((mz != 0).any()))
+az = rarray([0, 0, 0, 1, 0, 0, 0, 0], (2, 2, 2))
+case("any_3d", LR + ":93-101", "any", [t_in(az)], np.float64((az != 0).any()))
+mt = rmatrix([0, 1, 0, 0, 0, 0], 2, 3)
+case("any_transposed", LR + ":128-141", "any", [t_in(mt)], np.float64((mt.T != 0).any()), transpose=True)
+m6 = rmatrix([1, 0, 3, 4, 5, 6], 2, 3)
+case("all_transposed_zero", LR + ":264-288", "all", [t_in(m6)], np.float64((m6.T != 0).all()), transpose=True)
+a8 = rarray([1, 2, 0, 4, 5, 6, 7, 8], (2, 2, 2))
+case("all_3d_zero", LR + ":214-232", "all", [t_in(a8)], np.float64((a8 != 0).all()))
+
 
 def main():
     out = {"generator": "tests/golden/make_golden.py",

@@ -33,6 +33,9 @@ def run_oracle(case):
     if op in ("which.max", "which.min"):
         x = _transposed_view(xs[0]) if args.get("transpose") else oracle.View.of(xs[0])
         return oracle.arg_reduce("argmax" if op == "which.max" else "argmin", x, None, True)
+    if op in ("any", "all"):
+        x = _transposed_view(xs[0]) if args.get("transpose") else oracle.View.of(xs[0])
+        return np.asarray(oracle.reduce(op, x))
     if op in ("cumsum", "cumprod"):
         return oracle.scan(op, xs[0])
     if op in _OPS:
@@ -91,6 +94,10 @@ def run_gpu(acd, case):
     if op in ("which.max", "which.min"):
         x = acd.transpose_view(xs[0]) if args.get("transpose") else xs[0]
         return acd.which_max(x) if op == "which.max" else acd.which_min(x)
+    if op in ("any", "all"):
+        x = acd.transpose_view(xs[0]) if args.get("transpose") else xs[0]
+        r = getattr(acd, op)(x)
+        return np.float64(np.nan if r is None else float(r))
     if op in ("cumsum", "cumprod"):
         return getattr(acd, op)(xs[0]).as_array()
     if op in _OPS:

@@ -161,3 +161,39 @@ def test_keep_dims_shapes(acd):
     assert acd.tensor_sum(t, axis=[2], keep_dims=True).shape == (2, 1, 4)
     assert acd.tensor_sum(t, axis=[1, 3], keep_dims=True).shape == (1, 3, 1)
     assert acd.argmax(t, axis=3, keep_dims=True).shape == (2, 3, 1)
+
+
+@pytest.mark.parametrize("name,dt", [("float", np.float32), ("double", np.float64), ("int32", np.int32),
+                                     ("int64", np.int64), ("bool", np.bool_)])
+def test_any_all_three_valued(acd, name, dt):
+    """any / all with R's NA rules (NaN and INT_MIN integers are NA), over the
+    whole tensor and along axes, small and multi-CTA sizes, and a view."""
+    rng = np.random.default_rng(41)
+    na = {np.float32: np.nan, np.float64: np.nan, np.int32: np.iinfo(np.int32).min,
+          np.int64: np.iinfo(np.int64).min}.get(dt)
+
+    def check(x, t, what):
+        for op in ("any", "all"):
+            got = getattr(acd, op)(t)
+            exp = oracle.reduce(op, x)
+            assert (got is None and np.isnan(exp)) or (got is not None and float(got) == exp), (what, op, got, exp)
+            for ax in range(1, x.ndim + 1):
+                r = getattr(acd, op)(t, axis=[ax]).as_array().astype(np.float64)
+                r[r == np.iinfo(np.int32).min] = np.nan
+                e = np.asarray(oracle.reduce(op, x, [ax - 1]), dtype=np.float64)
+                assert np.array_equal(np.isnan(r), np.isnan(e)) and np.array_equal(r[~np.isnan(r)], e[~np.isnan(e)]), \
+                    (what, op, ax)
+
+    for shape in [(7,), (33, 40), (16, 300, 5), (2, 3000001)]:
+        base = (rng.random(shape) < 0.97)
+        x = base.astype(dt) if dt != np.bool_ else base
+        t = acd.as_tensor(x, dtype=name)
+        check(x, t, "%s mostly true" % (shape,))
+        y = np.ones(shape, dtype=dt)
+        if na is not None:
+            y.reshape(-1)[rng.integers(0, y.size, 3)] = na
+        check(y, acd.as_tensor(y, dtype=name), "%s ones with NA" % (shape,))
+        z = np.zeros(shape, dtype=dt)
+        check(z, acd.as_tensor(z, dtype=name), "%s zeros" % (shape,))
+    m = (rng.random((64, 48)) < 0.5).astype(dt) if dt != np.bool_ else rng.random((64, 48)) < 0.5
+    check(m.T, acd.transpose_view(acd.as_tensor(m, dtype=name)), "transposed view")
