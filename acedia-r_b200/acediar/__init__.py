@@ -11,4 +11,5 @@ from .tensor import (  # noqa: F401
     sum, sum_var, synchronize, tanh, tensor_count, tensor_max, tensor_mean, tensor_min, tensor_prod, tensor_sum,
     tensor_var, to_dtype, transpose, transpose_view, var, view, which_max, which_min, subset, assign, concat,
     concat_tensor, stack, stack_tensor, repeat_tensor, pad, pad_tensor, set_seed, rand_tensor, rnorm_tensor,
-    rand_tensor_uniform, rand_tensor_normal, runif, rnorm, any, all)
+    rand_tensor_uniform, rand_tensor_normal, runif, rnorm, any, all, diff, range_, is_finite, create_ones_like, all_equal,
+    tensor_pow)

@@ -496,6 +496,97 @@ concat = concat_tensor
 stack = stack_tensor
 
 
+def _flat_view(x, start, count):
+    """Elements start .. start+count-1 of a contiguous tensor, as a 1-D view."""
+    return gpuTensor(x.storage, (count,), x.dtype, (1,), x.offset + start)
+
+
+def diff(x, lag=1, differences=1):
+    """diff.gpuTensor (R/gpuTensor.R:2289-2333) on the device: base R's
+    diff(as.vector(x), lag, differences), each round one subtraction of two
+    offset views; a result of a multi-dimensional tensor is recycled to the
+    tensor's size and shape, as the reference does."""
+    if lag < 1:
+        raise ValueError("lag must be positive")
+    if differences < 1:
+        raise ValueError("differences must be positive")
+    d = contiguous(x) if not (x.is_contiguous()) else x
+    n = d.size
+    for _ in range(int(differences)):
+        m = n - int(lag)
+        if m <= 0:
+            raise ValueError("diff of single element tensor results in empty result - not supported by tensor system")
+        out = _alloc((m,), d.dtype, d.device)
+        L.check(L.lib().acd_binary(context(), L.BINARY["sub"], ctypes.byref(out.desc()),
+                                   ctypes.byref(_flat_view(d, int(lag), m).desc()),
+                                   ctypes.byref(_flat_view(d, 0, m).desc()), _stream()), "diff")
+        d, n = out, m
+    if x.ndims <= 1:
+        return d
+    full = _alloc(x.shape, x.dtype, x.device)  # rep_len(result, prod(shape))
+    pos, total = 0, x.size
+    while pos < total:
+        k = builtins.min(n, total - pos)
+        L.check(L.lib().acd_copy(context(), ctypes.byref(_flat_view(full, pos, k).desc()),
+                                 ctypes.byref(_flat_view(d, 0, k).desc()), _stream()), "diff")
+        pos += k
+    return full
+
+
+def range_(x):
+    """range.gpuTensor (R/gpuTensor.R:2216-2226): [min, max]."""
+    return [float(tensor_min(x).as_array().reshape(-1)[0]), float(tensor_max(x).as_array().reshape(-1)[0])]
+
+
+def is_finite(x):
+    """is.finite.gpuTensor (R/gpuTensor.R:1594-1596): TRUE when every element
+    is finite.  x - x is 0 exactly for finite x and NaN for +-Inf and NaN."""
+    if x.dtype in ("int32", "int64", "bool"):
+        return True
+    return bool(all((x - x) == 0))
+
+
+def all_equal(target, current, tolerance=1.5e-8):
+    """all.equal.gpuTensor (R/gpuTensor.R:1587-1591): base R's all.equal on
+    the host arrays — True, or a message naming the difference (mismatched
+    lengths, NA positions, or the mean relative / absolute difference above
+    `tolerance`)."""
+    t = np.asarray(target.as_array() if isinstance(target, gpuTensor) else target, dtype=np.float64)
+    c = np.asarray(current.as_array() if isinstance(current, gpuTensor) else current, dtype=np.float64)
+    if t.size != c.size:
+        return "Lengths (%d, %d) differ" % (t.size, c.size)
+    t, c = t.reshape(-1, order="F"), c.reshape(-1, order="F")
+    na_t, na_c = np.isnan(t), np.isnan(c)
+    if (na_t != na_c).any():
+        return "'is.NA' value mismatch: %d in current %d in target" % (na_c.sum(), na_t.sum())
+    t, c = t[~na_t], c[~na_t]
+    if t.size == 0:
+        return True
+    xy = np.abs(t - c).mean()
+    xn = np.abs(t).mean()
+    what = "absolute"
+    if np.isfinite(xn) and xn > tolerance:
+        xy, what = xy / xn, "relative"
+    if np.isnan(xy) or xy > tolerance:
+        return "Mean %s difference: %.7g" % (what, xy)
+    return True
+
+
+def create_ones_like(t):
+    """create_ones_like (R/gpuTensor.R:238-257): ones of t's shape and dtype,
+    filled on the device (the reference copies a host vector)."""
+    out = _alloc(t.shape, t.dtype, t.device)
+    L.check(L.lib().acd_fill(context(), ctypes.byref(out.desc()), ctypes.c_double(1.0), _stream()), "ones_like")
+    return out
+
+
+def tensor_pow(a, b):
+    """tensor_pow (R/gpuTensor.R:2123-2130): a^b elementwise with broadcasting."""
+    if not isinstance(a, gpuTensor) or not isinstance(b, gpuTensor):
+        raise ValueError("Both arguments must be gpuTensor objects")
+    return _arith("pow", a, b)
+
+
 # ---- random tensors (src/TensorRandom.cpp, R/gpuTensor.R:2342-2524) ---------
 # A counter-based stream: (seed, position).  Every call takes the next n
 # positions (rounded up to a multiple of 4).  set_seed makes runs repeatable;

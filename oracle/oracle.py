@@ -223,6 +223,26 @@ def pad(x, before, after, mode="constant", value=0.0):
     return np.pad(x, width, mode={"reflect": "symmetric", "replicate": "edge"}[mode])
 
 
+def diff(x, lag=1, differences=1):
+    """diff.gpuTensor (R/gpuTensor.R:2289-2333): base R's
+    diff(as.vector(x), lag, differences) on the column-major elements; for a
+    tensor of two or more axes the result is recycled (rep_len) to the
+    tensor's size and reshaped to its shape.  One rounding per difference."""
+    x = np.asarray(x)
+    if lag < 1:
+        raise ValueError("lag must be positive")
+    if differences < 1:
+        raise ValueError("differences must be positive")
+    v = x.reshape(-1, order="F")
+    for _ in range(int(differences)):
+        if v.size <= lag:
+            raise ValueError("diff of single element tensor results in empty result - not supported by tensor system")
+        v = v[lag:] - v[:-lag]
+    if x.ndim <= 1:
+        return v
+    return np.resize(v, x.size).reshape(x.shape, order="F")
+
+
 def gauss_chain(x, p=0.5):
     """x*p + exp(-(x^2)) with one rounding per R operator."""
     a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))

@@ -264,6 +264,69 @@ case("all_transposed_zero", LR + ":264-288", "all", [t_in(m6)], np.float64((m6.T
 a8 = rarray([1, 2, 0, 4, 5, 6, 7, 8], (2, 2, 2))
 case("all_3d_zero", LR + ":214-232", "all", [t_in(a8)], np.float64((a8 != 0).all()))
 
+# diff (tests/testthat/test-cumulative-operations.R): base R's diff(as.vector(x), lag, differences);
+# a matrix result is recycled to the matrix's shape (array(expected_vec, dim = dim(x)))
+CO = "tests/testthat/test-cumulative-operations.R"
+
+
+def r_diff(v, lag=1, differences=1):
+    v = np.asarray(v, dtype=np.float64).reshape(-1, order="F")
+    for _ in range(differences):
+        v = v[lag:] - v[:-lag]
+    return v
+
+
+d5 = [1, 4, 6, 8, 12]
+case("diff_1d", CO + ":168-180", "diff", [t_in(d5)], r_diff(d5))
+d6 = [1, 3, 6, 10, 15, 21]
+for lag, lines in [(1, "186-189"), (2, "191-194"), (3, "196-199")]:
+    case("diff_lag%d" % lag, CO + ":" + lines, "diff", [t_in(d6)], r_diff(d6, lag), lag=lag)
+d7 = [1, 2, 4, 7, 11, 16, 22]
+for k, lines in [(1, "206-209"), (2, "211-214"), (3, "216-219")]:
+    case("diff_differences%d" % k, CO + ":" + lines, "diff", [t_in(d7)], r_diff(d7, 1, k), differences=k)
+dd = [1.5, 3.2, 5.1, 7.8, 10.9]
+case("diff_f32", CO + ":222-231", "diff", [t_in(dd, "float")], r_diff(dd))
+case("diff_f64", CO + ":233-238", "diff", [t_in(dd, "double")], r_diff(dd))
+mdiff = rmatrix([1, 2, 4, 7, 11, 16], 2, 3)
+case("diff_matrix_recycled", CO + ":241-250", "diff", [t_in(mdiff)],
+     np.resize(r_diff(mdiff), mdiff.size).reshape(mdiff.shape, order="F"))
+case("diff_two", CO + ":253-256", "diff", [t_in([5, 8])], [3.0])
+case_error("diff_single", CO + ":258-263 (the reference's diff.gpuTensor stops: R/gpuTensor.R:2307-2312)", "diff",
+           [t_in([42])], "empty result")
+case("diff_negative", CO + ":265-269", "diff", [t_in([10, 7, 5, 8, 3])], r_diff([10, 7, 5, 8, 3]))
+for cid, lines, kw, pat in [("diff_lag0", "276", {"lag": 0}, "lag must be positive"),
+                            ("diff_lag_neg", "277", {"lag": -1}, "lag must be positive"),
+                            ("diff_differences0", "280", {"differences": 0}, "differences must be positive"),
+                            ("diff_differences_neg", "281", {"differences": -1}, "differences must be positive")]:
+    case_error(cid, CO + ":" + lines, "diff", [t_in([1, 2, 3, 4])], pat, **kw)
+
+# range (tests/testthat/test-range-extrema-helpers.R): c(min(x), max(x))
+RG = "tests/testthat/test-range-extrema-helpers.R"
+for cid, lines, data, dtype in [("range_1d", "25-36", [3, 1, 4, 1, 5, 9, 2, 6], "float"),
+                                ("range_f32", "38-46", [1.5, 2.7, 0.3, 4.9, 1.1], "float"),
+                                ("range_f64", "48-52", [1.5, 2.7, 0.3, 4.9, 1.1], "double"),
+                                ("range_single", "78-81", [42], "float"),
+                                ("range_same", "83-87", [3.14] * 5, "float"),
+                                ("range_negative", "89-93", [-5, -1, -10, -3, -7], "float"),
+                                ("range_mixed", "95-99", [-2, 5, -8, 3, 0, -1, 7], "float")]:
+    d = np.asarray(data, dtype=np.float64)
+    if dtype == "float":
+        d32 = d.astype(np.float32).astype(np.float64)  # the tensor holds float32 values
+        case(cid, RG + ":" + lines, "range", [t_in(d, dtype)], [d32.min(), d32.max()])
+    else:
+        case(cid, RG + ":" + lines, "range", [t_in(d, dtype)], [d.min(), d.max()])
+mr = rmatrix([3, 1, 4, 1, 5, 9, 2, 6, 5, 3, 5, 8], 3, 4)
+case("range_2d", RG + ":55-64", "range", [t_in(mr)], [mr.min(), mr.max()])
+
+# tensor_pow: sweep(base, 2, exp, "^") (test-comprehensive-broadcasting.R) and data_base ^ data_exp
+# (test-consolidated-core.R)
+pb = rmatrix([2, 3, 2, 3, 2, 3], 2, 3)
+pe = np.asarray([1.0, 2.0, 3.0])
+case("pow_broadcast_sweep", "tests/testthat/test-comprehensive-broadcasting.R:201-212", "tensor_pow",
+     [t_in(pb), t_in(pe)], r_sweep(pb, [2], pe, lambda a, b: a ** b))
+case("pow_elementwise", "tests/testthat/test-consolidated-core.R:356-366", "tensor_pow",
+     [t_in([2, 3, 4, 2, 3]), t_in([1, 2, 1, 3, 1])], np.asarray([2, 3, 4, 2, 3.0]) ** np.asarray([1, 2, 1, 3, 1.0]))
+
 
 def main():
     out = {"generator": "tests/golden/make_golden.py",

@@ -73,6 +73,13 @@ def run_oracle(case):
         else:
             y[sl] = xs[1]
         return y
+    if op == "diff":
+        return oracle.diff(xs[0], args.get("lag", 1), args.get("differences", 1))
+    if op == "range":
+        v = oracle.View.of(xs[0])
+        return np.asarray([oracle.reduce("min", v), oracle.reduce("max", v)], dtype=np.float64)
+    if op == "tensor_pow":
+        return oracle.binary("pow", xs[0], xs[1])
     if op == "mask_assign":
         y = xs[0].copy()
         m = np.asarray(args["mask"], dtype=bool).reshape(y.shape, order="F")
@@ -132,6 +139,12 @@ def run_gpu(acd, case):
         else:
             v = xs[1]
         return acd.assign(xs[0], *args["index"], value=v).as_array()
+    if op == "diff":
+        return acd.diff(xs[0], lag=args.get("lag", 1), differences=args.get("differences", 1)).as_array()
+    if op == "range":
+        return np.asarray(acd.range_(xs[0]), dtype=np.float64)
+    if op == "tensor_pow":
+        return acd.tensor_pow(xs[0], xs[1]).as_array()
     if op == "mask_assign":
         return acd.assign(xs[0], np.asarray(args["mask"], dtype=bool), value=args["value"]).as_array()
     raise KeyError(op)

@@ -178,9 +178,9 @@ def test_any_all_three_valued(acd, name, dt):
             exp = oracle.reduce(op, x)
             assert (got is None and np.isnan(exp)) or (got is not None and float(got) == exp), (what, op, got, exp)
             for ax in range(1, x.ndim + 1):
-                r = getattr(acd, op)(t, axis=[ax]).as_array().astype(np.float64)
+                r = getattr(acd, op)(t, axis=[ax]).as_array().astype(np.float64).reshape(-1)
                 r[r == np.iinfo(np.int32).min] = np.nan
-                e = np.asarray(oracle.reduce(op, x, [ax - 1]), dtype=np.float64)
+                e = np.asarray(oracle.reduce(op, x, [ax - 1]), dtype=np.float64).reshape(-1)
                 assert np.array_equal(np.isnan(r), np.isnan(e)) and np.array_equal(r[~np.isnan(r)], e[~np.isnan(e)]), \
                     (what, op, ax)
 
