@@ -12,4 +12,5 @@ from .tensor import (  # noqa: F401
     tensor_var, to_dtype, transpose, transpose_view, var, view, which_max, which_min, subset, assign, concat,
     concat_tensor, stack, stack_tensor, repeat_tensor, pad, pad_tensor, set_seed, rand_tensor, rnorm_tensor,
     rand_tensor_uniform, rand_tensor_normal, runif, rnorm, any, all, diff, range_, is_finite, create_ones_like, all_equal,
-    tensor_pow)
+    tensor_pow, permute, size, dim, as_vector, as_numeric, to_numeric, tensor_to_scalar, shares_memory, tensor_info,
+    set_random_seed, gpu_available, gpu_info, gpu_memory_available, gpu_status, gpu_add, gpu_multiply, gpu_scale, gpu_dot)

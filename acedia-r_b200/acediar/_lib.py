@@ -73,6 +73,9 @@ def _bind(lib):
     sigs = {
         "acd_version": ([], ctypes.c_char_p),
         "acd_last_error": ([], ctypes.c_char_p),
+        "acd_gpu_available": ([], i32),
+        "acd_gpu_info": ([ctypes.c_char_p, i64], i64),
+        "acd_gpu_memory_available": ([], f64),
         "acd_ctx_create": ([ctypes.c_int, P(vp)], i32),
         "acd_ctx_destroy": ([vp], i32),
         "acd_ctx_set_allocator": ([vp, vp, vp, vp], i32),

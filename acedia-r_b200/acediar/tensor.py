@@ -101,6 +101,17 @@ class gpuTensor:
         return "gpuTensor(shape=%s, dtype=%s%s)" % (self.shape, self.dtype,
                                                      "" if self.is_contiguous() else ", view")
 
+    def __str__(self):
+        """print.gpuTensor (R/gpuTensor.R:295-311): shape, device, dtype,
+        size, and the values when there are at most 100."""
+        lines = ["gpuTensor with shape %s " % " x ".join(str(s) for s in self.shape), "Device: CUDA",
+                 "DType: %s " % self.dtype, "Size: %d elements" % self.size]
+        if self.size <= 100:
+            lines += ["Data:", str(self.as_array())]
+        else:
+            lines.append("Use as.array() to view data")
+        return "\n".join(lines)
+
     # ---- transfer
     def as_array(self):
         """Host numpy array with R's column-major layout."""
@@ -862,3 +873,174 @@ def softmax(x, axis=None):
         st = L.lib().acd_softmax(context(), ctypes.byref(out.desc()), ctypes.byref(x.desc()), a, _stream())
     L.check(st, "softmax")
     return out
+
+
+# ---------------------------------------------------------------------------
+# host-side helpers of the R API (metadata, transfers, device queries)
+# ---------------------------------------------------------------------------
+def permute(tensor, dims):
+    """permute (R/gpuTensor.R:619-633): a zero-copy view with the axes in
+    `dims` order (1-based)."""
+    if len(dims) != tensor.ndims:
+        raise ValueError("Number of dimensions in 'dims' must match tensor dimensions")
+    return permute_view(tensor, dims)
+
+
+def size(tensor):
+    """size (R/gpuTensor.R:274-279): the number of elements."""
+    return tensor.size
+
+
+def dim(x):
+    """dim.gpuTensor (R/gpuTensor.R:844-846): the shape as integers."""
+    return [int(s) for s in x.shape]
+
+
+def as_vector(x):
+    """as.vector.gpuTensor (R/gpuTensor.R:187-190): the elements in
+    column-major order, in the tensor's dtype."""
+    return x.as_array().reshape(-1, order="F")
+
+
+def as_numeric(x):
+    """as.numeric.gpuTensor (R/gpuTensor.R:193-198): the elements in
+    column-major order as float64."""
+    return as_vector(x).astype(np.float64)
+
+
+def to_numeric(x):
+    """to_numeric (R/gpuTensor.R:202-208)."""
+    return as_numeric(x) if isinstance(x, gpuTensor) else np.asarray(x, dtype=np.float64).reshape(-1)
+
+
+def tensor_to_scalar(x):
+    """tensor_to_scalar (R/gpuTensor.R:218-230): the first element as a
+    number, with a warning when the tensor holds more than one."""
+    if not isinstance(x, gpuTensor):
+        raise ValueError("x must be a gpuTensor")
+    if x.size != 1:
+        import warnings
+        warnings.warn("Converting multi-element tensor to scalar, using first element")
+    first = gpuTensor(x.storage, (1,), x.dtype, (1,), x.offset)
+    return float(first.as_array().reshape(-1)[0])
+
+
+def shares_memory(tensor1, tensor2):
+    """shares_memory (R/gpuTensor.R:1524-1534).  The reference answers FALSE
+    always; here True when the two views address overlapping bytes of the
+    same device allocation (the span from each view's lowest to highest
+    element)."""
+    if not isinstance(tensor1, gpuTensor) or not isinstance(tensor2, gpuTensor):
+        raise ValueError("Both objects must be gpuTensors")
+    if tensor1.storage.untyped_storage().data_ptr() != tensor2.storage.untyped_storage().data_ptr():
+        return False
+
+    def span(t):
+        es = t.storage.element_size()
+        lo = hi = t.offset
+        for n, s in zip(t.shape, t.strides):
+            if n == 0:
+                return None
+            if s < 0:
+                lo += (n - 1) * s
+            else:
+                hi += (n - 1) * s
+        base = t.storage.data_ptr()
+        return base + lo * es, base + (hi + 1) * es
+
+    a, b = span(tensor1), span(tensor2)
+    return a is not None and b is not None and a[0] < b[1] and b[0] < a[1]
+
+
+def tensor_info(tensor):
+    """tensor_info (R/gpuTensor.R:1566-1577): shape, size, strides,
+    contiguity and dtype."""
+    if not isinstance(tensor, gpuTensor):
+        raise ValueError("Object is not a gpuTensor")
+    return {"shape": list(tensor.shape), "size": tensor.size, "strides": list(tensor.strides),
+            "is_contiguous": tensor.is_contiguous(), "dtype": tensor.dtype}
+
+
+def set_random_seed(seed):
+    """set_random_seed (src/TensorRandom.cpp:221-231): reseeds the random
+    stream used by rand_tensor / rnorm_tensor / runif / rnorm."""
+    set_seed(int(seed))
+
+
+def gpu_available():
+    """gpu_available (src/RcppInterface.cpp:7-9)."""
+    return bool(L.lib().acd_gpu_available())
+
+
+def gpu_info():
+    """gpu_info (src/RcppInterface.cpp:12-14): the device list as text."""
+    n = L.lib().acd_gpu_info(None, 0)
+    buf = ctypes.create_string_buffer(int(n) + 1)
+    L.lib().acd_gpu_info(buf, len(buf))
+    return buf.value.decode()
+
+
+def gpu_memory_available():
+    """gpu_memory_available (src/RcppInterface.cpp:17-20): free bytes."""
+    return float(L.lib().acd_gpu_memory_available())
+
+
+def gpu_status():
+    """gpu_status (R/gpu-utils.R:74-82)."""
+    free = gpu_memory_available()
+    ok = gpu_available()
+    return {"available": ok, "info": gpu_info(), "memory_available": free, "memory_gb": free / 1e9,
+            "recommended_use": ok and free > 1e9}
+
+
+def _vector_pair(a, b):
+    a = np.asarray(a, dtype=np.float64).reshape(-1)
+    b = np.asarray(b, dtype=np.float64).reshape(-1)
+    if a.size != b.size:
+        raise ValueError("Input vectors must have the same length")
+    return a, b
+
+
+def _device_only(force_cpu):
+    if force_cpu:
+        raise ValueError("force_cpu is not supported: this library computes on the device only")
+
+
+def gpu_add(a, b, force_cpu=False, warn_fallback=True):
+    """gpu_add (R/gpu_add.R:51-89): a + b of two numeric vectors through
+    float64 tensors.  The reference falls back to the CPU on error; here an
+    error propagates."""
+    _device_only(force_cpu)
+    a, b = _vector_pair(a, b)
+    if a.size == 0:
+        return np.zeros(0)
+    return as_vector(as_tensor(a) + as_tensor(b))
+
+
+def gpu_multiply(a, b, force_cpu=False, warn_fallback=True):
+    """gpu_multiply (R/gpu_multiply.R:51-88): a * b elementwise."""
+    _device_only(force_cpu)
+    a, b = _vector_pair(a, b)
+    if a.size == 0:
+        return np.zeros(0)
+    return as_vector(as_tensor(a) * as_tensor(b))
+
+
+def gpu_scale(x, scalar, force_cpu=False, warn_fallback=True):
+    """gpu_scale (R/gpu_multiply.R:127-163): x * scalar."""
+    _device_only(force_cpu)
+    if np.ndim(scalar) != 0 and np.size(scalar) != 1:
+        raise ValueError("scalar must be a single numeric value")
+    x = np.asarray(x, dtype=np.float64).reshape(-1)
+    if x.size == 0:
+        return np.zeros(0)
+    return as_vector(as_tensor(x) * float(np.asarray(scalar).reshape(-1)[0]))
+
+
+def gpu_dot(a, b, force_cpu=False, warn_fallback=True):
+    """gpu_dot (R/gpu_multiply.R:201-238): tensor_sum(a * b)."""
+    _device_only(force_cpu)
+    a, b = _vector_pair(a, b)
+    if a.size == 0:
+        return 0.0
+    return float(tensor_sum(as_tensor(a) * as_tensor(b)).as_array().reshape(-1)[0])

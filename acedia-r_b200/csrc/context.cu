@@ -7,6 +7,9 @@
 // control block of self-resetting counters, so no call allocates in steady state.
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
+#include <string>
+#include <algorithm>
 #include <mutex>
 
 #include "common.cuh"
@@ -231,6 +234,59 @@ using namespace acd;
 extern "C" {
 
 const char *acd_version(void) { return "acediar-b200 0.1 (sm_100a)"; }
+
+int32_t acd_gpu_available(void) {
+  int n = 0;
+  if (cudaGetDeviceCount(&n) != cudaSuccess || n == 0) {
+    cudaGetLastError();
+    return 0;
+  }
+  cudaDeviceProp prop;
+  if (cudaGetDeviceProperties(&prop, 0) != cudaSuccess) {
+    cudaGetLastError();
+    return 0;
+  }
+  return 1;
+}
+
+int64_t acd_gpu_info(char *buf, int64_t len) {
+  std::string info;
+  int n = 0;
+  const cudaError_t e = cudaGetDeviceCount(&n);
+  if (e != cudaSuccess) {
+    cudaGetLastError();
+    info = std::string("CUDA Error: ") + cudaGetErrorString(e);
+  } else if (n == 0) {
+    info = "No CUDA-capable devices found";
+  } else {
+    info = "Found " + std::to_string(n) + " CUDA device(s):\n";
+    for (int i = 0; i < n; ++i) {
+      cudaDeviceProp prop;
+      if (cudaGetDeviceProperties(&prop, i) != cudaSuccess) {
+        cudaGetLastError();
+        continue;
+      }
+      info += "  Device " + std::to_string(i) + ": " + prop.name + " (Compute " + std::to_string(prop.major) + "." +
+              std::to_string(prop.minor) + ") - " + std::to_string(prop.totalGlobalMem / (1024 * 1024)) + " MB\n";
+    }
+  }
+  if (buf && len > 0) {
+    const size_t k = std::min((size_t)(len - 1), info.size());
+    memcpy(buf, info.data(), k);
+    buf[k] = 0;
+  }
+  return (int64_t)info.size();
+}
+
+double acd_gpu_memory_available(void) {
+  if (!acd_gpu_available()) return 0.0;
+  size_t free_b = 0, total_b = 0;
+  if (cudaMemGetInfo(&free_b, &total_b) != cudaSuccess) {
+    cudaGetLastError();
+    return 0.0;
+  }
+  return (double)free_b;
+}
 
 const char *acd_last_error(void) { return g_err; }
 

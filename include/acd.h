@@ -129,6 +129,20 @@ const char *acd_version(void);
 const char *acd_last_error(void);
 const char *acd_status_string(acd_status s);
 
+/* Device queries, replacing gpu_available / gpu_info / gpu_memory_available
+ * (src/RcppInterface.cpp:7-20 over src/cuda_utils.h:17-103).  They need no
+ * context and do not fail: without a driver or a device they report 0 or a
+ * message.
+ *   acd_gpu_available          1 if device 0 answers a properties query
+ *   acd_gpu_info               "Found N CUDA device(s):\n" then one line
+ *                              "  Device i: <name> (Compute M.m) - <MiB> MB\n"
+ *                              per device; writes at most len-1 bytes plus a
+ *                              NUL into buf and returns the full length
+ *   acd_gpu_memory_available   free bytes on the current device */
+int32_t acd_gpu_available(void);
+int64_t acd_gpu_info(char *buf, int64_t len);
+double acd_gpu_memory_available(void);
+
 /* Creates a context on `device` (the current device is left unchanged). */
 acd_status acd_ctx_create(int device, acd_ctx **out);
 acd_status acd_ctx_destroy(acd_ctx *ctx);

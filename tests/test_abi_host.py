@@ -154,3 +154,23 @@ def test_column_major_strides():
     assert T.col_major_strides((3, 4, 5)) == (1, 3, 12)
     assert T._is_contig((3, 1, 5), (1, 7, 3))
     assert not T._is_contig((3, 4), (4, 1))
+
+
+def test_device_queries_answer_without_a_device(L):
+    """gpu_available / gpu_info / gpu_memory_available never fail: without a
+    usable driver they report 0 and a message."""
+    import ctypes
+    import torch
+    lib = L.lib()
+    n = lib.acd_gpu_info(None, 0)
+    buf = ctypes.create_string_buffer(int(n) + 1)
+    assert lib.acd_gpu_info(buf, len(buf)) == n and len(buf.value) == n
+    small = ctypes.create_string_buffer(5)
+    lib.acd_gpu_info(small, 5)
+    assert small.value == buf.value[:4]
+    if not torch.cuda.is_available():
+        assert lib.acd_gpu_available() == 0 and lib.acd_gpu_memory_available() == 0.0
+        assert buf.value.startswith(b"CUDA Error") or buf.value == b"No CUDA-capable devices found"
+    else:
+        assert lib.acd_gpu_available() == 1 and lib.acd_gpu_memory_available() > 0
+        assert buf.value.startswith(b"Found %d CUDA device(s):" % torch.cuda.device_count())

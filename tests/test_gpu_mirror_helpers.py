@@ -118,3 +118,54 @@ def test_all_equal(acd):
     msg = acd.all_equal(t, x + 1)
     assert isinstance(msg, str) and msg.startswith("Mean relative difference")
     assert acd.all_equal(t, np.ones(5)) == "Lengths (12, 5) differ"
+
+
+def test_metadata_and_transfer_helpers(acd):
+    x = np.arange(24, dtype=np.float64).reshape(2, 3, 4, order="F")
+    t = acd.as_tensor(x, dtype="double")
+    assert acd.size(t) == 24 and acd.dim(t) == [2, 3, 4]
+    np.testing.assert_array_equal(acd.as_vector(t), np.arange(24.0))
+    assert acd.as_numeric(acd.as_tensor(x, dtype="int32")).dtype == np.float64
+    p = acd.permute(t, [3, 1, 2])
+    assert p.shape == (4, 2, 3) and acd.shares_memory(p, t)
+    np.testing.assert_array_equal(p.as_array(), np.transpose(x, (2, 0, 1)))
+    with pytest.raises(ValueError, match="must match tensor dimensions"):
+        acd.permute(t, [1, 2])
+    info = acd.tensor_info(p)
+    assert info["shape"] == [4, 2, 3] and info["size"] == 24 and info["is_contiguous"] is False
+    assert not acd.shares_memory(t, acd.as_tensor(x, dtype="double"))
+    import acediar.tensor as T
+    v = acd.as_tensor(np.arange(100.0), dtype="double")
+    assert not acd.shares_memory(T._slice_view(v, [0], [50]), T._slice_view(v, [50], [50]))
+    assert acd.shares_memory(T._slice_view(v, [0], [51]), T._slice_view(v, [50], [50]))
+    assert acd.tensor_to_scalar(acd.as_tensor(np.array([7.5]), dtype="float")) == 7.5
+    with pytest.warns(UserWarning, match="using first element"):
+        assert acd.tensor_to_scalar(v) == 0.0
+    s = str(acd.as_tensor(np.ones((2, 2)), dtype="float"))
+    assert s.startswith("gpuTensor with shape 2 x 2") and "Data:" in s
+    assert "Use as.array() to view data" in str(acd.as_tensor(np.ones(101), dtype="float"))
+
+
+def test_device_queries_and_seed(acd):
+    st = acd.gpu_status()
+    assert st["available"] is True and st["memory_available"] > 1e9 and st["info"].startswith("Found ")
+    acd.set_random_seed(123)
+    a = acd.rand_tensor((1000,), dtype="double").as_array()
+    acd.set_random_seed(123)
+    b = acd.rand_tensor((1000,), dtype="double").as_array()
+    np.testing.assert_array_equal(a, b)
+
+
+def test_legacy_vector_wrappers(acd):
+    rng = np.random.default_rng(16)
+    a, b = rng.normal(0, 1, 100001), rng.normal(0, 1, 100001)
+    np.testing.assert_array_equal(acd.gpu_add(a, b), a + b)
+    np.testing.assert_array_equal(acd.gpu_multiply(a, b), a * b)
+    np.testing.assert_array_equal(acd.gpu_scale(a, 2.5), a * 2.5)
+    d = acd.gpu_dot(a, b)
+    assert abs(d - float(np.dot(a, b))) <= 1e-12 * float(np.abs(a * b).sum())
+    assert acd.gpu_dot([], []) == 0.0 and acd.gpu_add([], []).size == 0
+    with pytest.raises(ValueError, match="same length"):
+        acd.gpu_add([1.0, 2.0], [1.0])
+    with pytest.raises(ValueError, match="device only"):
+        acd.gpu_add([1.0], [2.0], force_cpu=True)
