@@ -49,6 +49,8 @@ def parse():
     ap.add_argument("--workload", default="views", choices=["views", "c1", "c2", "c3", "c4"],
                     help="views (default, the sharded strided-views step) or a per-op report of one of the "
                          "other configurations on one GPU")
+    ap.add_argument("--only", default=None,
+                    help="per-op reports: time only the ops whose name contains this text (e.g. 'var(T, axis=2)')")
     return ap.parse_args()
 
 
@@ -227,10 +229,16 @@ def _time_graph(fn, reps=10, replays=5):
     return e0.elapsed_time(e1) / (replays * reps)
 
 
+_ONLY = None  # --only: time just the ops whose name contains this text
+
+
 def _op(name, fn, nbytes, peak, reps=10, note=None, graph=False):
     """Times `fn`.  graph=True (calls that return device tensors) reports the
     device time from CUDA-graph replay as `ms` and the eager per-call time,
-    host wrapper included, as `eager_ms`."""
+    host wrapper included, as `eager_ms`.  Returns None for an op that --only
+    leaves out."""
+    if _ONLY is not None and _ONLY not in name:
+        return None
     eager = _time(fn, reps)
     ms = _time_graph(fn, reps) if graph else eager
     gbs = nbytes / (ms * 1e-3) / 1e9
@@ -249,6 +257,8 @@ def run_config_report(a):
     import acediar as acd
     import acediar.tensor as Tm
 
+    global _ONLY
+    _ONLY = a.only
     torch.cuda.set_device(0)
     peak, peak_kind = peaks()
     g = torch.Generator(device="cuda")
@@ -347,11 +357,13 @@ def run_config_report(a):
         Xd = acd.from_torch(torch.randn(R2 * C2, generator=g, device="cuda", dtype=torch.float64), (R2, C2), "double")
         ops.append(_op("softmax f64 1024x32768 axis=2", lambda: acd.softmax(Xd, axis=2), 2 * 8 * R2 * C2, peak))
         ops.append(_op("softmax f32 whole tensor", lambda: acd.softmax(Xf), 3 * 4 * R * C, peak))
-        sm = acd.softmax(Xf, axis=2)
-        rows = acd.tensor_sum(sm, axis=[2]).as_array()
-        ops.append({"op": "row sums of f32 softmax", "max_abs_dev_from_1": float(np.abs(rows - 1).max())})
+        if _ONLY is None or _ONLY in "row sums of f32 softmax":
+            sm = acd.softmax(Xf, axis=2)
+            rows = acd.tensor_sum(sm, axis=[2]).as_array()
+            ops.append({"op": "row sums of f32 softmax", "max_abs_dev_from_1": float(np.abs(rows - 1).max())})
         workload = "row softmax float32 65536x4096 (N(0,4) + row offset U(-50,50)), float64 1024x32768"
         unit_elems = R * C
+    ops = [o for o in ops if o is not None]
     line = {"metric": "HBM GB/s per op (algorithmic bytes / CUDA-event time)", "workload": workload,
             "peak_GB/s": peak, "peak_source": peak_kind, "ops": ops, "n_gpus": 1}
     print(json.dumps(line), flush=True)
