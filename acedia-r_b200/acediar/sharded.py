@@ -13,6 +13,9 @@ other ranks:
     (2^32-1 - global index) with the sign bit flipped, and a MAX all-reduce
     picks the largest value and, among equal values, the smallest index — the
     reference's first-index rule (src/kernels/tensor_kernels.cu:794).
+The statistics row and the keys can come from the pass that writes the
+elementwise chain (chain_stats_keys), or from the pass that also makes the
+contiguous copy (permute_chain_stats_keys), so no output is re-read.
 There is no peer-memory access and no multicast: the exchanged bytes are a few
 doubles and one key per output (1 MiB at 256 x 512).
 """
@@ -99,6 +102,38 @@ def argmax_keys(x, axis0, index_base):
     L.check(L.lib().acd_argmax_keys(context(), ctypes.c_void_p(keys.data_ptr()), ctypes.byref(x.desc()), axis0,
                                     int(index_base), _stream()), "argmax_keys")
     return keys, kept
+
+
+def chain_stats_keys(y, p0, index_base):
+    """z = y*p0 + exp(-(y^2)) together with this shard's statistics row of z
+    and the argmax keys of z along axis 1 (R's 1-based axis; the global index
+    offset is `index_base`), from one pass over z: the same three results as
+    fused(), stats_partial() and argmax_keys(), without reading z again."""
+    z = _alloc(y.shape, y.dtype, y.device)
+    stats = torch.empty(STATS_WIDTH, dtype=torch.float64, device=y.device)
+    n = int(np.prod(y.shape[1:])) if y.ndims > 1 else 1
+    keys = torch.empty(n, dtype=torch.int64, device=y.device)
+    L.check(L.lib().acd_fused_stats_keys(context(), ctypes.byref(z.desc()), ctypes.byref(y.desc()), float(p0),
+                                         ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(keys.data_ptr()),
+                                         int(index_base), _stream()), "fused_stats_keys")
+    return z, stats, keys
+
+
+def permute_chain_stats_keys(x, p0, index_base):
+    """y = contiguous(x) of the permuted view x, z = y*p0 + exp(-(y^2)), the
+    statistics row of z and its argmax keys along axis 1, from one read of x
+    when x is a matrix transpose (the permute_view(x, c(3, 1, 2)) of the
+    strided-views step)."""
+    y = _alloc(x.shape, x.dtype, x.device)
+    z = _alloc(x.shape, x.dtype, x.device)
+    stats = torch.empty(STATS_WIDTH, dtype=torch.float64, device=x.device)
+    n = int(np.prod(x.shape[1:])) if x.ndims > 1 else 1
+    keys = torch.empty(n, dtype=torch.int64, device=x.device)
+    L.check(L.lib().acd_permute_fused_stats_keys(context(), ctypes.byref(y.desc()), ctypes.byref(z.desc()),
+                                                 ctypes.byref(x.desc()), float(p0), ctypes.c_void_p(stats.data_ptr()),
+                                                 ctypes.c_void_p(keys.data_ptr()), int(index_base), _stream()),
+            "permute_fused_stats_keys")
+    return y, z, stats, keys
 
 
 def decode_keys(keys, shape, one_based=True, dtype="int32"):

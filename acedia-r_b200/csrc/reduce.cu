@@ -22,7 +22,9 @@
 //   (src/kernels/tensor_ops.cu:850-880), global argmin scans 256 elements
 //   (src/kernels/tensor_kernels.cu:1224-1309); both become device reductions.
 #include "common.cuh"
+#include "ops.cuh"
 #include "reduce_acc.cuh"
+#include "tma.cuh"
 
 namespace acd {
 
@@ -396,6 +398,77 @@ __global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(cons
     }
     if (threadIdx.x == 0) counters[it + itiles * o] = 0u;
   }
+}
+
+// ---- the elementwise chain with its statistics and argmax keys, one pass ----
+// z = x*p + exp(-(x^2)) over a contiguous float32 tensor whose axis 0 (the
+// argmax axis) has F elements, F a multiple of 4: a CTA takes whole fibers
+// (F consecutive elements) in turn, writes z with 16-byte stores, keeps its
+// threads' shifted moments of z (shift K = z[0], as acd_stats_partial) across
+// all its fibers, and reduces each fiber's argmax to one key (as
+// acd_argmax_keys).  The moments meet in finish_grid.  z is read by nothing
+// else, so the step moves 8 bytes per element instead of 16.
+constexpr int kChainThreads = 256;
+
+template <int U>
+__global__ void __launch_bounds__(kChainThreads) k_chain_stats_keys(const float *__restrict__ x, float *__restrict__ z,
+                                                                    int64_t F, int64_t nfib, float p,
+                                                                    VarAcc<float> *__restrict__ partials,
+                                                                    unsigned int *counter, OutSpec os_stats,
+                                                                    long long *__restrict__ keys, int64_t index_base) {
+  __shared__ VarAcc<float> smem_st[kChainThreads / 32];
+  __shared__ ArgAcc<float, true> smem_arg[kChainThreads / 32];
+  const FusedScaleAddExpNegSquare<float> f{p};
+  const float K = f(x[0]);
+  VarAcc<float> st;
+  st.init();
+  st.set_shift(K);
+  OutSpec os_key;
+  os_key.mode = kModeKey;
+  os_key.out = keys;
+  os_key.index_base = index_base;
+  const int64_t nv = F / 4;
+  const int64_t bd = blockDim.x;
+  for (int64_t fb = blockIdx.x; fb < nfib; fb += gridDim.x) {
+    const Vec<float, 4> *xi = reinterpret_cast<const Vec<float, 4> *>(x + fb * F);
+    Vec<float, 4> *zo = reinterpret_cast<Vec<float, 4> *>(z + fb * F);
+    ArgAcc<float, true> am;
+    am.init();
+    int64_t v = threadIdx.x;
+    for (; v + (U - 1) * bd < nv; v += U * bd) {  // U vectors in flight, unguarded
+      Vec<float, 4> a[U];
+#pragma unroll
+      for (int u = 0; u < U; ++u) a[u] = xi[v + u * bd];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        Vec<float, 4> r;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) r.v[k] = f(a[u].v[k]);
+        zo[v + u * bd] = r;
+        const int64_t i0 = (v + u * bd) * 4;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          st.add(r.v[k], 0);
+          am.add(r.v[k], i0 + k);
+        }
+      }
+    }
+    for (; v < nv; v += bd) {
+      const Vec<float, 4> a = xi[v];
+      Vec<float, 4> r;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) r.v[k] = f(a.v[k]);
+      zo[v] = r;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        st.add(r.v[k], 0);
+        am.add(r.v[k], v * 4 + k);
+      }
+    }
+    block_reduce(am, smem_arg);
+    if (threadIdx.x == 0) am.store(os_key, fb);
+  }
+  finish_grid(st, smem_st, partials, counter, os_stats, 0, K);
 }
 
 // ---- generic: any set of reduced axes, a warp per output --------------------
@@ -908,6 +981,85 @@ acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const
                                      n, one_based ? 1 : 0);
   ACD_CUDA(cudaGetLastError());
   return ACD_OK;
+}
+
+acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, double p0, double *stats,
+                                int64_t *keys, int64_t index_base, acd_stream stream) {
+  if (!ctx || !stats || !keys) return fail(ACD_ERR_INVALID, "acd_fused_stats_keys: null argument");
+  ACD_TRY(check_desc(out, "out"));
+  ACD_TRY(check_desc(in, "in"));
+  if (in->dtype != ACD_FLOAT32 || out->dtype != ACD_FLOAT32)
+    return fail(ACD_ERR_DTYPE, "acd_fused_stats_keys: float32 input and output required");
+  if (in->ndim < 1) return fail(ACD_ERR_SHAPE, "acd_fused_stats_keys: at least one axis required");
+  if (out->ndim != in->ndim) return fail(ACD_ERR_SHAPE, "acd_fused_stats_keys: output shape differs");
+  for (int d = 0; d < in->ndim; ++d)
+    if (out->shape[d] != in->shape[d]) return fail(ACD_ERR_SHAPE, "acd_fused_stats_keys: output shape differs");
+  const int64_t n = desc_numel(in);
+  if (n == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_fused_stats_keys: empty input");
+  const int64_t F = in->shape[0];
+  if (index_base < 0 || index_base + F > 0xFFFFFFFFLL)
+    return fail(ACD_ERR_INVALID, "acd_fused_stats_keys: global index must fit in 32 bits");
+  const bool fast = desc_is_contiguous(in) && desc_is_contiguous(out) && F % 4 == 0 &&
+                    aligned_to<float>(desc_ptr(in), 16) && aligned_to<float>(desc_ptr(out), 16);
+  if (!fast) {  // the three separate passes
+    ACD_TRY(acd_fused(ctx, ACD_FUSED_SCALE_ADD_EXP_NEG_SQUARE, out, in, nullptr, p0, stream));
+    ACD_TRY(acd_stats_partial(ctx, stats, out, stream));
+    return acd_argmax_keys(ctx, keys, out, 0, index_base, stream);
+  }
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t nfib = n / F;
+  const int grid = persistent_grid(ctx, k_chain_stats_keys<4>, kChainThreads, 0, nfib);
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, align_up(sizeof(VarAcc<float>) * grid, 256), s, &scratch));
+  OutSpec os;
+  os.mode = kModeStats;
+  os.out = stats;
+  os.op = ACD_RED_VAR;
+  os.n = n;
+  k_chain_stats_keys<4><<<grid, kChainThreads, 0, s>>>(
+      reinterpret_cast<const float *>(desc_ptr(in)), reinterpret_cast<float *>(desc_ptr(out)), F, nfib, (float)p0,
+      static_cast<VarAcc<float> *>(scratch), &ctx->control->counters[0], os, reinterpret_cast<long long *>(keys),
+      index_base);
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const acd_desc *z, const acd_desc *in,
+                                        double p0, double *stats, int64_t *keys, int64_t index_base,
+                                        acd_stream stream) {
+  if (!ctx || !stats || !keys) return fail(ACD_ERR_INVALID, "acd_permute_fused_stats_keys: null argument");
+  ACD_TRY(check_desc(y, "y"));
+  ACD_TRY(check_desc(z, "z"));
+  ACD_TRY(check_desc(in, "in"));
+  if (in->dtype != ACD_FLOAT32 || y->dtype != ACD_FLOAT32 || z->dtype != ACD_FLOAT32)
+    return fail(ACD_ERR_DTYPE, "acd_permute_fused_stats_keys: float32 views required");
+  if (!desc_is_contiguous(y) || !desc_is_contiguous(z))
+    return fail(ACD_ERR_UNSUPPORTED, "acd_permute_fused_stats_keys: y and z must be contiguous");
+  if (y->ndim != in->ndim || z->ndim != in->ndim)
+    return fail(ACD_ERR_SHAPE, "acd_permute_fused_stats_keys: y, z and in must have one shape");
+  for (int d = 0; d < in->ndim; ++d)
+    if (y->shape[d] != in->shape[d] || z->shape[d] != in->shape[d])
+      return fail(ACD_ERR_SHAPE, "acd_permute_fused_stats_keys: y, z and in must have one shape");
+  const int64_t n = desc_numel(in);
+  if (n == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_permute_fused_stats_keys: empty input");
+  const int64_t n0 = in->shape[0];
+  if (index_base < 0 || index_base + n0 > 0xFFFFFFFFLL)
+    return fail(ACD_ERR_INVALID, "acd_permute_fused_stats_keys: global index must fit in 32 bits");
+  // one kernel when `in` is a matrix transpose: axes 1.. contiguous in order
+  // (the permute_view(x, c(3, 1, 2)) of a contiguous x), axis 0 strided
+  bool fast = in->ndim >= 2 && in->stride[1] == 1;
+  for (int d = 2; fast && d < in->ndim; ++d) fast = in->stride[d] == in->stride[d - 1] * in->shape[d - 1];
+  if (fast) {
+    DeviceGuard g(ctx->device);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (launch_transpose_chain_tma4(ctx, reinterpret_cast<float *>(desc_ptr(y)), reinterpret_cast<float *>(desc_ptr(z)),
+                                    reinterpret_cast<const float *>(desc_ptr(in)), n0, n / n0, in->stride[0],
+                                    (float)p0, stats, keys, index_base, s))
+      return ACD_OK;
+  }
+  ACD_TRY(acd_copy(ctx, y, in, stream));
+  return acd_fused_stats_keys(ctx, z, y, p0, stats, keys, index_base, stream);
 }
 
 }  // extern "C"

@@ -299,6 +299,28 @@ acd_status acd_stats_partial(acd_ctx *ctx, double *stats, const acd_desc *in, ac
  * index_base.  FLOAT32 input only. */
 acd_status acd_argmax_keys(acd_ctx *ctx, int64_t *keys, const acd_desc *in, int32_t axis,
                            int64_t index_base, acd_stream stream);
+/* The elementwise chain out = in*p0 + exp(-(in^2)) (bit-identical to
+ * acd_fused with ACD_FUSED_SCALE_ADD_EXP_NEG_SQUARE) together with, from the
+ * same pass over out, the statistics row of acd_stats_partial(out) and the
+ * keys of acd_argmax_keys(out, axis 0, index_base).  It replaces those three
+ * calls on the strided-views step (R/gpuTensor.R:2032-2042 for x^2 and the
+ * Ops group; src/kernels/tensor_ops.cu:785-880 for the statistics and the
+ * argmax): out is still written, but not read again.  FLOAT32.  Contiguous,
+ * 16-byte aligned data with shape[0] a multiple of 4 take one kernel; other
+ * views run the three calls. */
+acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, double p0, double *stats,
+                                int64_t *keys, int64_t index_base, acd_stream stream);
+/* y = contiguous(in) for the permuted view `in` together with everything
+ * acd_fused_stats_keys(z, y, ...) produces, from one read of the input: the
+ * strided-views step's permute -> contiguous, elementwise chain, statistics
+ * row and argmax keys (R/gpuTensor.R:1544-1556 and src/gpuTensor.h:723-769 for
+ * the copy).  y and z are contiguous FLOAT32 of in's shape.  When in is a
+ * matrix transpose (axes 1.. contiguous in order, axis 0 strided, 16-byte
+ * aligned, shape[0] a multiple of 4, both extents >= 64) one TMA kernel does
+ * it all; other views run acd_copy then acd_fused_stats_keys. */
+acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const acd_desc *z, const acd_desc *in,
+                                        double p0, double *stats, int64_t *keys, int64_t index_base,
+                                        acd_stream stream);
 /* Decodes keys back to indices (INT32/INT64 out, 1-based when one_based). */
 acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const int64_t *keys,
                                   int32_t one_based, acd_stream stream);

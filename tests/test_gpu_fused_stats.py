@@ -1,0 +1,88 @@
+"""The one-pass forms of the strided-views step against the separate calls
+they replace.  acd_fused_stats_keys (the elementwise chain with its
+statistics row and argmax keys) and acd_permute_fused_stats_keys (that, plus
+the permute -> contiguous copy, from one read of the input): y and z
+bit-identical, keys identical to acd_argmax_keys, the statistics row's n and
+shift identical and its moments within 1e-12 relative, and the merged
+sum/var within the float32 contract of the oracle."""
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from helpers import assert_exact
+
+pytestmark = pytest.mark.gpu
+
+
+def _merged(stats):
+    import acediar.sharded as SH
+    tot, var = SH.merge_stats_torch(stats.view(1, -1))
+    return float(tot.item()), float(var.item())
+
+
+def _check_stats(st, st_ref, z_ref):
+    assert st[0] == st_ref[0] and st[1] == st_ref[1], (st, st_ref)
+    scale = np.abs(z_ref.astype(np.float64) - st_ref[1])
+    assert abs(st[2] - st_ref[2]) <= 1e-12 * max(1.0, scale.sum())
+    assert abs(st[3] - st_ref[3]) <= 1e-12 * max(1.0, (scale ** 2).sum())
+
+
+@pytest.mark.parametrize("shape,base", [((4096, 16, 8), 0), ((32768, 3, 5), 7), ((8, 1000), 0), ((4, 1), 12345),
+                                        ((1024, 700), 2 ** 31), ((6, 10), 0), ((4100, 33), 5)])
+def test_fused_stats_keys_matches_separate_calls(acd, shape, base):
+    import acediar.sharded as SH
+    rng = np.random.default_rng(sum(shape) + base)
+    x = (np.round(rng.normal(0, 1, shape) * 4) / 4).astype(np.float32)  # quarters: ties inside fibers
+    y = acd.as_tensor(x, dtype="float")
+    z, stats, keys = SH.chain_stats_keys(y, 0.5, base)
+    z_ref = acd.fused("scale_add_exp_neg_square", y, p0=0.5)
+    assert_exact(z.as_array(), z_ref.as_array(), "z")
+    keys_ref, _ = SH.argmax_keys(z_ref, 0, base)
+    assert torch.equal(keys.cpu(), keys_ref.cpu()), "argmax keys"
+    zz = z_ref.as_array()
+    _check_stats(stats.cpu().numpy(), SH.stats_partial(z_ref).cpu().numpy(), zz)
+    tot, var = _merged(stats)
+    e_tot = float(oracle.reduce("sum", oracle.View.of(zz)))
+    e_var = float(oracle.reduce("var", oracle.View.of(zz)))
+    assert abs(tot - e_tot) <= 1e-5 * max(1.0, np.abs(zz.astype(np.float64)).sum())
+    if zz.size > 1:
+        assert abs(var - e_var) <= 1e-5 * abs(e_var)
+    idx = SH.decode_keys(keys, shape[1:] if len(shape) > 1 else (1,), one_based=True, dtype="int64").as_array()
+    exp_idx = np.argmax(zz, axis=0) + 1 + base
+    assert_exact(idx, exp_idx.astype(np.int64).reshape(idx.shape), "decoded argmax")
+
+
+def test_fused_stats_keys_view_falls_back(acd):
+    """A permuted (non-contiguous) input runs the three separate passes."""
+    import acediar.sharded as SH
+    x = np.random.default_rng(3).normal(size=(64, 48)).astype(np.float32)
+    v = acd.transpose_view(acd.as_tensor(x, dtype="float"))
+    z, stats, keys = SH.chain_stats_keys(v, 0.5, 0)
+    zc = acd.fused("scale_add_exp_neg_square", acd.contiguous(v), p0=0.5)
+    assert_exact(z.as_array(), zc.as_array(), "z of a view")
+    keys_ref, _ = SH.argmax_keys(zc, 0, 0)
+    assert torch.equal(keys.cpu(), keys_ref.cpu())
+
+
+@pytest.mark.parametrize("xshape,base", [((64, 32, 256), 0), ((128, 64, 4096), 9), ((100, 3, 72), 0),
+                                         ((256, 5, 1000), 3 * 2 ** 30), ((64, 64, 130), 0), ((8, 8, 16), 0),
+                                         ((96, 1, 64), 1)])
+def test_permute_fused_stats_keys_matches_separate_calls(acd, xshape, base):
+    """Tile-aligned, ragged (i and j), and fallback shapes (extent not a
+    multiple of 4, or below one 64 x 64 tile); two calls in a row, since the
+    atomic keys and the statistics counter must start clean each call."""
+    import acediar.sharded as SH
+    rng = np.random.default_rng(sum(xshape) + base)
+    x = (np.round(rng.normal(0, 1, xshape) * 8) / 8).astype(np.float32)  # eighths: ties inside fibers
+    xv = acd.permute_view(acd.as_tensor(x, dtype="float"), [3, 1, 2])
+    for rep in range(2):
+        y, z, stats, keys = SH.permute_chain_stats_keys(xv, 0.5, base)
+        y_ref = acd.contiguous(xv)
+        assert_exact(y.as_array(), y_ref.as_array(), "y")
+        z_ref = acd.fused("scale_add_exp_neg_square", y_ref, p0=0.5)
+        assert_exact(z.as_array(), z_ref.as_array(), "z")
+        keys_ref, _ = SH.argmax_keys(z_ref, 0, base)
+        assert torch.equal(keys.cpu(), keys_ref.cpu()), ("keys", rep)
+        _check_stats(stats.cpu().numpy(), SH.stats_partial(z_ref).cpu().numpy(), z_ref.as_array())
+    acd.check_device_status()
