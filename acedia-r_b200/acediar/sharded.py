@@ -14,8 +14,8 @@ other ranks:
     picks the largest value and, among equal values, the smallest index — the
     reference's first-index rule (src/kernels/tensor_kernels.cu:794).
 The statistics row and the keys can come from the pass that writes the
-elementwise chain (chain_stats_keys), or from the pass that also makes the
-contiguous copy (permute_chain_stats_keys), so no output is re-read.
+elementwise chain (chain_stats_keys; permute_chain_stats_keys adds the
+contiguous copy in front), so z is written once and not re-read.
 There is no peer-memory access and no multicast: the exchanged bytes are a few
 doubles and one key per output (1 MiB at 256 x 512).
 """
@@ -120,10 +120,9 @@ def chain_stats_keys(y, p0, index_base):
 
 
 def permute_chain_stats_keys(x, p0, index_base):
-    """y = contiguous(x) of the permuted view x, z = y*p0 + exp(-(y^2)), the
-    statistics row of z and its argmax keys along axis 1, from one read of x
-    when x is a matrix transpose (the permute_view(x, c(3, 1, 2)) of the
-    strided-views step)."""
+    """y = contiguous(x) of the permuted view x, then z = y*p0 + exp(-(y^2)),
+    the statistics row of z and its argmax keys along axis 1 from one pass
+    over y: the strided-views step in one call (two kernels)."""
     y = _alloc(x.shape, x.dtype, x.device)
     z = _alloc(x.shape, x.dtype, x.device)
     stats = torch.empty(STATS_WIDTH, dtype=torch.float64, device=x.device)

@@ -24,7 +24,6 @@
 #include "common.cuh"
 #include "ops.cuh"
 #include "reduce_acc.cuh"
-#include "tma.cuh"
 
 namespace acd {
 
@@ -402,11 +401,15 @@ __global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(cons
 
 // ---- the elementwise chain with its statistics and argmax keys, one pass ----
 // z = x*p + exp(-(x^2)) over a contiguous float32 tensor whose axis 0 (the
-// argmax axis) has F elements, F a multiple of 4: a CTA takes whole fibers
-// (F consecutive elements) in turn, writes z with 16-byte stores, keeps its
-// threads' shifted moments of z (shift K = z[0], as acd_stats_partial) across
-// all its fibers, and reduces each fiber's argmax to one key (as
-// acd_argmax_keys).  The moments meet in finish_grid.  z is read by nothing
+// argmax axis) has F elements, F a multiple of 4.  Each warp takes whole
+// fibers (F consecutive elements) in turn: it writes z with 16-byte stores,
+// keeps each thread's running argmax of the fiber (its indices only grow, so
+// a strict > keeps the first of equal values; an all -inf fiber takes its
+// first element, as the argmax reduction does; NaN never wins) and reduces it to one key per
+// fiber (as acd_argmax_keys) with shuffles only.  The threads' shifted moments
+// of z (shift K = z[0], as acd_stats_partial) run across all their fibers and
+// meet in finish_grid.  No block-wide barrier until the end, so the loads of
+// one fiber follow the previous one's without a drain; z is read by nothing
 // else, so the step moves 8 bytes per element instead of 16.
 constexpr int kChainThreads = 256;
 
@@ -417,7 +420,6 @@ __global__ void __launch_bounds__(kChainThreads) k_chain_stats_keys(const float 
                                                                     unsigned int *counter, OutSpec os_stats,
                                                                     long long *__restrict__ keys, int64_t index_base) {
   __shared__ VarAcc<float> smem_st[kChainThreads / 32];
-  __shared__ ArgAcc<float, true> smem_arg[kChainThreads / 32];
   const FusedScaleAddExpNegSquare<float> f{p};
   const float K = f(x[0]);
   VarAcc<float> st;
@@ -427,33 +429,38 @@ __global__ void __launch_bounds__(kChainThreads) k_chain_stats_keys(const float 
   os_key.mode = kModeKey;
   os_key.out = keys;
   os_key.index_base = index_base;
+  const int lane = threadIdx.x & 31;
   const int64_t nv = F / 4;
-  const int64_t bd = blockDim.x;
-  for (int64_t fb = blockIdx.x; fb < nfib; fb += gridDim.x) {
+  const int64_t gw = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nw = ((int64_t)gridDim.x * blockDim.x) >> 5;
+  for (int64_t fb = gw; fb < nfib; fb += nw) {
     const Vec<float, 4> *xi = reinterpret_cast<const Vec<float, 4> *>(x + fb * F);
     Vec<float, 4> *zo = reinterpret_cast<Vec<float, 4> *>(z + fb * F);
     ArgAcc<float, true> am;
     am.init();
-    int64_t v = threadIdx.x;
-    for (; v + (U - 1) * bd < nv; v += U * bd) {  // U vectors in flight, unguarded
+    int64_t v = lane;
+    for (; v + 32 * (U - 1) < nv; v += 32 * U) {  // U vectors in flight, unguarded
       Vec<float, 4> a[U];
 #pragma unroll
-      for (int u = 0; u < U; ++u) a[u] = xi[v + u * bd];
+      for (int u = 0; u < U; ++u) a[u] = xi[v + 32 * u];
 #pragma unroll
       for (int u = 0; u < U; ++u) {
         Vec<float, 4> r;
 #pragma unroll
         for (int k = 0; k < 4; ++k) r.v[k] = f(a[u].v[k]);
-        zo[v + u * bd] = r;
-        const int64_t i0 = (v + u * bd) * 4;
+        zo[v + 32 * u] = r;
+        const int64_t i0 = (v + 32 * u) * 4;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
           st.add(r.v[k], 0);
-          am.add(r.v[k], i0 + k);
+          if (r.v[k] > am.v || (r.v[k] == am.v && am.i == LLONG_MAX)) {  // first -inf too
+            am.v = r.v[k];
+            am.i = i0 + k;
+          }
         }
       }
     }
-    for (; v < nv; v += bd) {
+    for (; v < nv; v += 32) {
       const Vec<float, 4> a = xi[v];
       Vec<float, 4> r;
 #pragma unroll
@@ -462,11 +469,14 @@ __global__ void __launch_bounds__(kChainThreads) k_chain_stats_keys(const float 
 #pragma unroll
       for (int k = 0; k < 4; ++k) {
         st.add(r.v[k], 0);
-        am.add(r.v[k], v * 4 + k);
+        if (r.v[k] > am.v || (r.v[k] == am.v && am.i == LLONG_MAX)) {
+          am.v = r.v[k];
+          am.i = v * 4 + k;
+        }
       }
     }
-    block_reduce(am, smem_arg);
-    if (threadIdx.x == 0) am.store(os_key, fb);
+    warp_reduce(am);
+    if (lane == 0) am.store(os_key, fb);
   }
   finish_grid(st, smem_st, partials, counter, os_stats, 0, K);
 }
@@ -1009,7 +1019,7 @@ acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_des
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t nfib = n / F;
-  const int grid = persistent_grid(ctx, k_chain_stats_keys<4>, kChainThreads, 0, nfib);
+  const int grid = persistent_grid(ctx, k_chain_stats_keys<4>, kChainThreads, 0, (nfib + 7) / 8);
   void *scratch;
   ACD_TRY(get_scratch(ctx, align_up(sizeof(VarAcc<float>) * grid, 256), s, &scratch));
   OutSpec os;
@@ -1043,21 +1053,10 @@ acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const a
       return fail(ACD_ERR_SHAPE, "acd_permute_fused_stats_keys: y, z and in must have one shape");
   const int64_t n = desc_numel(in);
   if (n == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_permute_fused_stats_keys: empty input");
-  const int64_t n0 = in->shape[0];
-  if (index_base < 0 || index_base + n0 > 0xFFFFFFFFLL)
+  if (index_base < 0 || index_base + in->shape[0] > 0xFFFFFFFFLL)
     return fail(ACD_ERR_INVALID, "acd_permute_fused_stats_keys: global index must fit in 32 bits");
-  // one kernel when `in` is a matrix transpose: axes 1.. contiguous in order
-  // (the permute_view(x, c(3, 1, 2)) of a contiguous x), axis 0 strided
-  bool fast = in->ndim >= 2 && in->stride[1] == 1;
-  for (int d = 2; fast && d < in->ndim; ++d) fast = in->stride[d] == in->stride[d - 1] * in->shape[d - 1];
-  if (fast) {
-    DeviceGuard g(ctx->device);
-    cudaStream_t s = static_cast<cudaStream_t>(stream);
-    if (launch_transpose_chain_tma4(ctx, reinterpret_cast<float *>(desc_ptr(y)), reinterpret_cast<float *>(desc_ptr(z)),
-                                    reinterpret_cast<const float *>(desc_ptr(in)), n0, n / n0, in->stride[0],
-                                    (float)p0, stats, keys, index_base, s))
-      return ACD_OK;
-  }
+  // the copy (TMA transpose for a permuted matrix), then the chain with its
+  // statistics and keys in one pass over the copy
   ACD_TRY(acd_copy(ctx, y, in, stream));
   return acd_fused_stats_keys(ctx, z, y, p0, stats, keys, index_base, stream);
 }

@@ -102,12 +102,4 @@ bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, co
 bool launch_transpose_tma4(acd_ctx *ctx, void *out, const void *in, int64_t n0, int64_t n1, int64_t n2,
                            int64_t os1, int64_t os2, int64_t is0, int64_t is2, cudaStream_t stream);
 
-// The transpose y = in^T of a float32 matrix (n0 x n1 out, contiguous along
-// i; in contiguous along j with row stride is0) together with z = y*p +
-// exp(-(y^2)), the statistics row of z and the argmax keys of z along i.
-// Returns false (nothing launched) when the shapes or alignment do not fit.
-bool launch_transpose_chain_tma4(acd_ctx *ctx, float *y, float *z, const float *in, int64_t n0, int64_t n1,
-                                 int64_t is0, float p, double *stats, int64_t *keys, int64_t index_base,
-                                 cudaStream_t stream);
-
 }  // namespace acd

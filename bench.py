@@ -30,11 +30,11 @@ N0, N1, N2 = 256, 512, 32768
 CHUNK = 128  # shards hold whole multiples of 128 slices along axis 3
 SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
-BYTES_PER_ELEM = {"transpose": 8, "fused_chain": 8, "stats": 4, "argmax_keys": 4}
-# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 13
+BYTES_PER_ELEM = {"transpose": 8, "chain_stats_keys": 8}
+# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 5-13
 # launches) on the 256x512x1024 case of the same step, scaled by elements to a full launch.  Reads are
 # exactly 4 B/elem; the write side reads low by the ~48 MB of dirty lines still in L2 when a launch ends.
-TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.638, "fused_chain": 7.639, "stats": 4.001, "argmax_keys": 4.008}
+TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.638, "chain_stats_keys": 7.676}
 
 
 def parse():
@@ -428,23 +428,19 @@ def main():
     def k_transpose(s, dx=None):
         L.check(lib.acd_copy(ctx, pref(d_y), pref(dx if dx is not None else d_xp), s), "copy")
 
-    def k_chain(s):
-        L.check(lib.acd_fused(ctx, 0, pref(d_z), pref(d_y), None, ctypes.c_double(0.5), s), "fused")
-
-    def k_stats(s):
-        L.check(lib.acd_stats_partial(ctx, ctypes.c_void_p(stats.data_ptr()), pref(d_z), s), "stats")
-
-    def k_keys(s):
-        L.check(lib.acd_argmax_keys(ctx, ctypes.c_void_p(keys.data_ptr()), pref(d_z), 0, lo, s), "keys")
+    def k_chain_stats_keys(s):
+        # z = y*0.5 + exp(-y^2), with this shard's statistics row of z and the
+        # argmax keys of z along axis 1 from the same pass (z is not re-read)
+        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5),
+                                         ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(keys.data_ptr()), lo, s),
+                "fused_stats_keys")
 
     def step(dx=None, input_read=None):
         s = stream()
         k_transpose(s, dx)
         if input_read is not None:
             input_read.record()  # the transpose is the only reader of the input
-        k_chain(s)
-        k_stats(s)
-        k_keys(s)
+        k_chain_stats_keys(s)
         if world > 1:
             dist.all_gather_into_tensor(gathered, stats)
             dist.all_reduce(keys, op=dist.ReduceOp.MAX)
@@ -455,7 +451,7 @@ def main():
         L.check(lib.acd_argmax_keys_decode(ctx, pref(d_idx), ctypes.c_void_p(keys.data_ptr()), 1, s), "decode")
         return tot, var
 
-    LAUNCHES_PER_STEP = 5
+    LAUNCHES_PER_STEP = 3  # transpose, chain with statistics and keys, key decode
 
     def barrier():
         torch.cuda.synchronize()
@@ -489,8 +485,7 @@ def main():
 
     # ---- per-kernel durations (CUDA events on the launching stream)
     kern = {}
-    for name, fn in [("transpose", k_transpose), ("fused_chain", k_chain), ("stats", k_stats),
-                     ("argmax_keys", k_keys)]:
+    for name, fn in [("transpose", k_transpose), ("chain_stats_keys", k_chain_stats_keys)]:
         for _ in range(2):
             fn(stream())
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]

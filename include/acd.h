@@ -310,14 +310,11 @@ acd_status acd_argmax_keys(acd_ctx *ctx, int64_t *keys, const acd_desc *in, int3
  * views run the three calls. */
 acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, double p0, double *stats,
                                 int64_t *keys, int64_t index_base, acd_stream stream);
-/* y = contiguous(in) for the permuted view `in` together with everything
- * acd_fused_stats_keys(z, y, ...) produces, from one read of the input: the
- * strided-views step's permute -> contiguous, elementwise chain, statistics
- * row and argmax keys (R/gpuTensor.R:1544-1556 and src/gpuTensor.h:723-769 for
- * the copy).  y and z are contiguous FLOAT32 of in's shape.  When in is a
- * matrix transpose (axes 1.. contiguous in order, axis 0 strided, 16-byte
- * aligned, shape[0] a multiple of 4, both extents >= 64) one TMA kernel does
- * it all; other views run acd_copy then acd_fused_stats_keys. */
+/* y = contiguous(in) for the view `in`, then z, the statistics row and the
+ * argmax keys of acd_fused_stats_keys(z, y, ...): the strided-views step's
+ * permute -> contiguous (R/gpuTensor.R:1544-1556, src/gpuTensor.h:723-769),
+ * elementwise chain, statistics and argmax keys as one call of two kernels.
+ * y and z are contiguous FLOAT32 of in's shape. */
 acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const acd_desc *z, const acd_desc *in,
                                         double p0, double *stats, int64_t *keys, int64_t index_base,
                                         acd_stream stream);

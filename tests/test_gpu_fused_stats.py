@@ -1,7 +1,7 @@
 """The one-pass forms of the strided-views step against the separate calls
 they replace.  acd_fused_stats_keys (the elementwise chain with its
-statistics row and argmax keys) and acd_permute_fused_stats_keys (that, plus
-the permute -> contiguous copy, from one read of the input): y and z
+statistics row and argmax keys) and acd_permute_fused_stats_keys (the
+permute -> contiguous copy followed by that): y and z
 bit-identical, keys identical to acd_argmax_keys, the statistics row's n and
 shift identical and its moments within 1e-12 relative, and the merged
 sum/var within the float32 contract of the oracle."""
@@ -69,9 +69,10 @@ def test_fused_stats_keys_view_falls_back(acd):
                                          ((256, 5, 1000), 3 * 2 ** 30), ((64, 64, 130), 0), ((8, 8, 16), 0),
                                          ((96, 1, 64), 1)])
 def test_permute_fused_stats_keys_matches_separate_calls(acd, xshape, base):
-    """Tile-aligned, ragged (i and j), and fallback shapes (extent not a
-    multiple of 4, or below one 64 x 64 tile); two calls in a row, since the
-    atomic keys and the statistics counter must start clean each call."""
+    """Transposes the TMA copy takes (tile-aligned and ragged) and ones it
+    does not (an extent not a multiple of 4, or below one 64 x 64 tile), with
+    and without the chain kernel's one-pass form; two calls in a row, since
+    the statistics counter must start clean each call."""
     import acediar.sharded as SH
     rng = np.random.default_rng(sum(xshape) + base)
     x = (np.round(rng.normal(0, 1, xshape) * 8) / 8).astype(np.float32)  # eighths: ties inside fibers
@@ -86,3 +87,23 @@ def test_permute_fused_stats_keys_matches_separate_calls(acd, xshape, base):
         assert torch.equal(keys.cpu(), keys_ref.cpu()), ("keys", rep)
         _check_stats(stats.cpu().numpy(), SH.stats_partial(z_ref).cpu().numpy(), z_ref.as_array())
     acd.check_device_status()
+
+
+def test_fused_stats_keys_infinities_and_nan(acd):
+    """Fibers that are all -inf (the first element wins, as in the argmax
+    reduction), a fiber with NaN (NaN never wins; the moments turn NaN, as in
+    acd_stats_partial), and +inf."""
+    import acediar.sharded as SH
+    x = np.random.default_rng(4).normal(size=(64, 6)).astype(np.float32)
+    x[:, 0] = -np.inf
+    x[5, 1] = np.nan
+    x[7, 2] = np.inf
+    x[:, 3] = -np.inf
+    x[9, 3] = 2.0
+    y = acd.as_tensor(x, dtype="float")
+    z, stats, keys = SH.chain_stats_keys(y, 0.5, 3)
+    z_ref = acd.fused("scale_add_exp_neg_square", y, p0=0.5)
+    np.testing.assert_array_equal(z.as_array(), z_ref.as_array())  # NaN in the same place counts as equal
+    keys_ref, _ = SH.argmax_keys(z_ref, 0, 3)
+    assert torch.equal(keys.cpu(), keys_ref.cpu()), (keys.cpu(), keys_ref.cpu())
+    assert np.isnan(stats.cpu().numpy()[2]) and np.isnan(SH.stats_partial(z_ref).cpu().numpy()[2])
