@@ -1019,7 +1019,7 @@ acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_des
   DeviceGuard g(ctx->device);
   cudaStream_t s = static_cast<cudaStream_t>(stream);
   const int64_t nfib = n / F;
-  const int grid = persistent_grid(ctx, k_chain_stats_keys<4>, kChainThreads, 0, (nfib + 7) / 8);
+  const int grid = persistent_grid(ctx, k_chain_stats_keys<8>, kChainThreads, 0, (nfib + 7) / 8);
   void *scratch;
   ACD_TRY(get_scratch(ctx, align_up(sizeof(VarAcc<float>) * grid, 256), s, &scratch));
   OutSpec os;
@@ -1027,7 +1027,7 @@ acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_des
   os.out = stats;
   os.op = ACD_RED_VAR;
   os.n = n;
-  k_chain_stats_keys<4><<<grid, kChainThreads, 0, s>>>(
+  k_chain_stats_keys<8><<<grid, kChainThreads, 0, s>>>(
       reinterpret_cast<const float *>(desc_ptr(in)), reinterpret_cast<float *>(desc_ptr(out)), F, nfib, (float)p0,
       static_cast<VarAcc<float> *>(scratch), &ctx->control->counters[0], os, reinterpret_cast<long long *>(keys),
       index_base);
