@@ -31,10 +31,10 @@ CHUNK = 128  # shards hold whole multiples of 128 slices along axis 3
 SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
 BYTES_PER_ELEM = {"transpose": 8, "chain_stats_keys": 8}
-# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 5-13
+# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 11
 # launches) on the 256x512x1024 case of the same step, scaled by elements to a full launch.  Reads are
 # exactly 4 B/elem; the write side reads low by the ~48 MB of dirty lines still in L2 when a launch ends.
-TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.638, "chain_stats_keys": 7.676}
+TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.601, "chain_stats_keys": 7.645}
 
 
 def parse():
