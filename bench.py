@@ -255,6 +255,7 @@ def run_config_report(a):
     import torch
 
     import acediar as acd
+    import acediar._lib as L
     import acediar.tensor as Tm
 
     global _ONLY
@@ -329,7 +330,16 @@ def run_config_report(a):
         B = 4 * n
         for op in ("sum", "mean", "var", "max"):
             ops.append(_op("%s(T)" % op, (lambda op=op: getattr(acd, "tensor_" + op)(T)), B, peak))
-        ops.append(_op("sum+var fused", lambda: acd.sum_var(T), B, peak, note="includes two 8-byte D2H reads"))
+        sv_s, sv_v = Tm._alloc((1,), "double"), Tm._alloc((1,), "double")
+        sv_d = (sv_s.desc(), sv_v.desc(), T.desc())
+
+        def sum_var_device():
+            L.check(L.lib().acd_sum_var(Tm.context(), ctypes.byref(sv_d[0]), ctypes.byref(sv_d[1]),
+                                        ctypes.byref(sv_d[2]), Tm._stream()), "sum_var")
+        ops.append(_op("sum+var fused", sum_var_device, B, peak, graph=True,
+                       note="device outputs; acd.sum_var() adds two 8-byte host reads"))
+        ops.append(_op("sum+var fused, host result", lambda: acd.sum_var(T), B, peak,
+                       note="includes two synchronising 8-byte D2H reads"))
         ops.append(_op("which.max(T)", lambda: Tm._arg("argmax", T), B, peak))
         ops.append(_op("as.double(T)", lambda: acd.to_dtype(T, "double"), B + 2 * B, peak, graph=True))
         ops.append(_op("rnorm_tensor(4096x4096x16)", lambda: acd.rnorm_tensor(shp), B, peak, graph=True,
