@@ -297,15 +297,26 @@ __global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(cons
   const T *base = in + o * so;
 
   Acc acc[V];
-#pragma unroll
-  for (int k = 0; k < V; ++k) {
-    acc[k].init();
-    if constexpr (Acc::kShift) {
-      if (i0 + k < I) acc[k].set_shift(base[(i0 + k) * si]);
-    }
-  }
   const bool full = VEC && (i0 + V <= I);
   int64_t r = r0 + wr;
+  // the shift is row 0 of each output: a thread whose first row is row 0
+  // takes it from that row's load, others load it as one vector
+  bool need_shift = false;
+#pragma unroll
+  for (int k = 0; k < V; ++k) acc[k].init();
+  if constexpr (Acc::kShift) {
+    if (full && r == 0 && r < r1) {
+      need_shift = true;
+    } else if (full) {
+      const Vec<T, V> k0 = *reinterpret_cast<const Vec<T, V> *>(base + i0);
+#pragma unroll
+      for (int k = 0; k < V; ++k) acc[k].set_shift(k0.v[k]);
+    } else {
+#pragma unroll
+      for (int k = 0; k < V; ++k)
+        if (i0 + k < I) acc[k].set_shift(base[(i0 + k) * si]);
+    }
+  }
   if (full) {
     // RU rows in flight per thread; accumulation stays in row order.  The
     // loop is not unrolled further, so the register bound, not unrolling,
@@ -316,6 +327,13 @@ __global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(cons
       Vec<T, V> x[RU];
 #pragma unroll
       for (int u = 0; u < RU; ++u) x[u] = *reinterpret_cast<const Vec<T, V> *>(base + (r + u * WR) * sr + i0);
+      if constexpr (Acc::kShift) {
+        if (need_shift) {  // x[0] is row 0
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc[k].set_shift(x[0].v[k]);
+          need_shift = false;
+        }
+      }
 #pragma unroll
       for (int u = 0; u < RU; ++u) {
 #pragma unroll
@@ -328,6 +346,13 @@ __global__ void __launch_bounds__(256, outer_min_blocks<Acc>()) k_red_outer(cons
     const T *row = base + r * sr;
     if (full) {
       const Vec<T, V> x = *reinterpret_cast<const Vec<T, V> *>(row + i0);
+      if constexpr (Acc::kShift) {
+        if (need_shift) {  // this row is row 0
+#pragma unroll
+          for (int k = 0; k < V; ++k) acc[k].set_shift(x.v[k]);
+          need_shift = false;
+        }
+      }
 #pragma unroll
       for (int k = 0; k < V; ++k) acc[k].add(x.v[k], r);
     } else {
