@@ -184,30 +184,44 @@ static long double binary(int op, long double a, long double b, int dt) {
 }
 
 /* ---- elementwise ------------------------------------------------------- */
+/* The *_range forms compute output elements lo..hi-1 only (the config-size
+ * checks split the outputs over threads); the plain forms compute all. */
+void orc_unary_range(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, void *out,
+                     int64_t lo, int64_t hi) {
+  for (int64_t i = lo; i < hi; ++i) put(out, dt, i, unary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), dt));
+}
+
 void orc_unary(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, void *out) {
-  const int64_t n = numel(nd, shape);
-  for (int64_t i = 0; i < n; ++i) put(out, dt, i, unary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), dt));
+  orc_unary_range(op, dt, in, nd, shape, st, out, 0, numel(nd, shape));
 }
 
 /* a and b carry strides already expanded to `shape` (stride 0 on broadcast
  * dims); out_dt is the input dtype or bool for comparisons */
-void orc_binary(int op, int dt, const void *a, const int64_t *sa, const void *b, const int64_t *sb, int nd,
-                const int64_t *shape, int out_dt, void *out) {
-  const int64_t n = numel(nd, shape);
-  for (int64_t i = 0; i < n; ++i) {
+void orc_binary_range(int op, int dt, const void *a, const int64_t *sa, const void *b, const int64_t *sb, int nd,
+                      const int64_t *shape, int out_dt, void *out, int64_t lo, int64_t hi) {
+  for (int64_t i = lo; i < hi; ++i) {
     const long double x = ld_get(a, dt, offset_of(i, nd, shape, sa));
     const long double y = ld_get(b, dt, offset_of(i, nd, shape, sb));
     put(out, out_dt, i, binary(op, x, y, dt));
   }
 }
 
+void orc_binary(int op, int dt, const void *a, const int64_t *sa, const void *b, const int64_t *sb, int nd,
+                const int64_t *shape, int out_dt, void *out) {
+  orc_binary_range(op, dt, a, sa, b, sb, nd, shape, out_dt, out, 0, numel(nd, shape));
+}
+
 /* x op s, with s first cast to the tensor dtype */
+void orc_scalar_range(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, double s,
+                      int out_dt, void *out, int64_t lo, int64_t hi) {
+  const long double sv = rnd((long double)s, dt);
+  for (int64_t i = lo; i < hi; ++i)
+    put(out, out_dt, i, binary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), sv, dt));
+}
+
 void orc_scalar(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, double s,
                 int out_dt, void *out) {
-  const int64_t n = numel(nd, shape);
-  const long double sv = rnd((long double)s, dt);
-  for (int64_t i = 0; i < n; ++i)
-    put(out, out_dt, i, binary(op, ld_get(in, dt, offset_of(i, nd, shape, st)), sv, dt));
+  orc_scalar_range(op, dt, in, nd, shape, st, s, out_dt, out, 0, numel(nd, shape));
 }
 
 /* x*p + exp(-(x^2)), five roundings */
@@ -426,16 +440,17 @@ static void split(int nd, const int64_t *shape, const int64_t *st, uint32_t mask
   }
 }
 
-/* out (double) holds one value per kept element */
-int orc_reduce(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, uint32_t mask,
-               double *out) {
+/* out (double) holds one value per kept element; outputs o_lo..o_hi-1 are
+ * computed (the multithreaded checks split the outputs over threads) */
+int orc_reduce_range(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st,
+                     uint32_t mask, double *out, int64_t o_lo, int64_t o_hi) {
   int nk, nr;
   int64_t ks[MAXD], kst[MAXD], rs[MAXD], rst[MAXD];
   split(nd, shape, st, mask, &nk, ks, kst, &nr, rs, rst);
-  const int64_t O = numel(nk, ks), R = numel(nr, rs);
+  const int64_t R = numel(nr, rs);
   long double *v = (long double *)malloc(sizeof(long double) * (R > 0 ? R : 1));
   if (!v) return -1;
-  for (int64_t o = 0; o < O; ++o) {
+  for (int64_t o = o_lo; o < o_hi; ++o) {
     const int64_t base = offset_of(o, nk, ks, kst);
     for (int64_t j = 0; j < R; ++j) v[j] = ld_get(in, dt, base + offset_of(j, nr, rs, rst));
     if (op == R_ANY || op == R_ALL) {
@@ -460,15 +475,25 @@ int orc_reduce(int op, int dt, const void *in, int nd, const int64_t *shape, con
   return 0;
 }
 
-/* first index of the max (min); NaN never wins; -1 when none */
-int orc_arg_reduce(int is_max, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
-                   int one_based, int64_t *out) {
+int orc_reduce(int op, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, uint32_t mask,
+               double *out) {
+  int nk, nr;
+  int64_t ks[MAXD], kst[MAXD], rs[MAXD], rst[MAXD];
+  split(nd, shape, st, mask, &nk, ks, kst, &nr, rs, rst);
+  return orc_reduce_range(op, dt, in, nd, shape, st, mask, out, 0, numel(nk, ks));
+}
+
+/* first index of the max (min); NaN never wins; -1 when none.  Outputs
+ * o_lo..o_hi-1 (o_hi < 0: all). */
+int orc_arg_reduce_range(int is_max, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st,
+                         int axis, int one_based, int64_t *out, int64_t o_lo, int64_t o_hi) {
   const uint32_t mask = axis < 0 ? 0xFFu : (1u << axis);
   int nk, nr;
   int64_t ks[MAXD], kst[MAXD], rs[MAXD], rst[MAXD];
   split(nd, shape, st, mask, &nk, ks, kst, &nr, rs, rst);
   const int64_t O = numel(nk, ks), R = numel(nr, rs);
-  for (int64_t o = 0; o < O; ++o) {
+  if (o_hi < 0 || o_hi > O) o_hi = O;
+  for (int64_t o = o_lo; o < o_hi; ++o) {
     const int64_t base = offset_of(o, nk, ks, kst);
     int64_t best = -1;
     long double bv = 0.0L;
@@ -485,6 +510,14 @@ int orc_arg_reduce(int is_max, int dt, const void *in, int nd, const int64_t *sh
   return 0;
 }
 
+int orc_arg_reduce(int is_max, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
+                   int one_based, int64_t *out) {
+  return orc_arg_reduce_range(is_max, dt, in, nd, shape, st, axis, one_based, out, 0, -1);
+}
+
+int orc_scan_fibers(int is_prod, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
+                    void *out, int64_t f_lo, int64_t f_hi);
+
 /* cumsum/cumprod along `axis` (axis < 0: flattened column-major) */
 int orc_scan(int is_prod, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
              void *out) {
@@ -498,13 +531,22 @@ int orc_scan(int is_prod, int dt, const void *in, int nd, const int64_t *shape, 
     }
     return 0;
   }
+  return orc_scan_fibers(is_prod, dt, in, nd, shape, st, axis, out, 0, -1);
+}
+
+/* cumsum/cumprod along `axis` >= 0 of fibers f_lo..f_hi-1 (f_hi < 0: all);
+ * fiber f starts at output index (f % ostride) + (f / ostride) * ostride * R */
+int orc_scan_fibers(int is_prod, int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis,
+                    void *out, int64_t f_lo, int64_t f_hi) {
+  const int64_t n = numel(nd, shape);
   /* out is contiguous: stride of `axis` in out = prod(shape[<axis]) */
   int64_t ostride = 1;
   for (int d = 0; d < axis; ++d) ostride *= shape[d];
   const int64_t R = shape[axis];
-  for (int64_t i = 0; i < n; ++i) {
-    const int64_t r = (i / ostride) % R;
-    if (r != 0) continue; /* start of a fiber */
+  const int64_t F = R > 0 ? n / R : 0;
+  if (f_hi < 0 || f_hi > F) f_hi = F;
+  for (int64_t f = f_lo; f < f_hi; ++f) {
+    const int64_t i = (f % ostride) + (f / ostride) * ostride * R;
     long double acc = is_prod ? 1.0L : 0.0L;
     for (int64_t k = 0; k < R; ++k) {
       const int64_t oi = i + k * ostride;
@@ -518,7 +560,8 @@ int orc_scan(int is_prod, int dt, const void *in, int nd, const int64_t *shape, 
 
 /* softmax along `axis` (axis < 0: whole tensor); exp in long double of the
  * dtype-rounded difference, sum in long double */
-int orc_softmax(int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis, void *out) {
+int orc_softmax_fibers(int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis, void *out,
+                       int64_t f_lo, int64_t f_hi) {
   const int64_t n = numel(nd, shape);
   if (n == 0) return 0;
   int64_t ostride = 1, R = n;
@@ -526,11 +569,14 @@ int orc_softmax(int dt, const void *in, int nd, const int64_t *shape, const int6
     for (int d = 0; d < axis; ++d) ostride *= shape[d];
     R = shape[axis];
   }
+  if (R == 0) return 0;
+  const int64_t F = n / R;
+  if (f_hi < 0 || f_hi > F) f_hi = F;
   long double *e = (long double *)malloc(sizeof(long double) * R);
   if (!e) return -1;
-  for (int64_t i = 0; i < n; ++i) {
-    if (axis >= 0 && (i / ostride) % R != 0) continue;
-    if (axis < 0 && i != 0) break;
+  for (int64_t f = f_lo; f < f_hi; ++f) {
+    /* fiber f starts at (f % ostride) + (f / ostride) * ostride * R */
+    const int64_t i = (f % ostride) + (f / ostride) * ostride * R;
     const int64_t step = axis >= 0 ? ostride : 1;
     long double m = -INFINITY;
     for (int64_t k = 0; k < R; ++k) m = fmaxl_r(m, ld_get(in, dt, offset_of(i + k * step, nd, shape, st)));
@@ -544,6 +590,10 @@ int orc_softmax(int dt, const void *in, int nd, const int64_t *shape, const int6
   }
   free(e);
   return 0;
+}
+
+int orc_softmax(int dt, const void *in, int nd, const int64_t *shape, const int64_t *st, int axis, void *out) {
+  return orc_softmax_fibers(dt, in, nd, shape, st, axis, out, 0, -1);
 }
 
 /* Fused sum and var of a contiguous array (for large-size checks and the CPU

@@ -12,6 +12,7 @@ The broadcast rule is restated here from the reference (src/gpuTensor.h:248-340,
 src/TensorArithmetic.cpp:240-292): the shorter shape is tried at every offset
 from the leading side and the first fit wins.
 """
+import concurrent.futures as cf
 import ctypes
 import os
 import subprocess
@@ -133,11 +134,30 @@ def broadcast_strides(shape, strides, out_shape):
 
 
 # ---------------------------------------------------------------------------
-def unary(op, x):
+def _ranges(n, threads, fn):
+    """Runs fn(lo, hi) over `threads` consecutive output ranges.  ctypes
+    releases the GIL inside the C call, so the ranges run in parallel."""
+    threads = max(1, min(int(threads), n)) if n > 0 else 1
+    if threads == 1:
+        fn(0, n)
+        return
+    bounds = [(n * k // threads, n * (k + 1) // threads) for k in range(threads)]
+    with cf.ThreadPoolExecutor(threads) as ex:
+        list(ex.map(lambda b: fn(*b), bounds))
+
+
+def default_threads():
+    return os.cpu_count() or 1
+
+
+def unary(op, x, threads=1):
     v = View.of(x)
-    out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
-    lib().orc_unary(UNARY[op], DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
-                    out.ctypes.data_as(ctypes.c_void_p))
+    n = int(np.prod(v.shape))
+    out = np.empty(n, dtype=v.dtype)
+    sh, st = _arr(v.shape), _arr(v.strides)
+    _ranges(n, threads, lambda lo, hi: lib().orc_unary_range(
+        UNARY[op], DT[v.dtype], v.ptr(), len(v.shape), sh, st, out.ctypes.data_as(ctypes.c_void_p),
+        ctypes.c_int64(lo), ctypes.c_int64(hi)))
     return _result(out, v.shape)
 
 
@@ -145,24 +165,30 @@ def copy(x):
     return unary("copy", x)
 
 
-def binary(op, a, b, out_dtype=None):
+def binary(op, a, b, out_dtype=None, threads=1):
     va, vb = View.of(a), View.of(b)
     shape = broadcast_shape(va.shape, vb.shape)
     sa = broadcast_strides(va.shape, va.strides, shape)
     sb = broadcast_strides(vb.shape, vb.strides, shape)
     odt = np.dtype(out_dtype) if out_dtype is not None else (np.dtype(np.uint8) if op in COMPARE else va.dtype)
-    out = np.empty(int(np.prod(shape)), dtype=odt)
-    lib().orc_binary(BINARY[op], DT[va.dtype], va.ptr(), _arr(sa), vb.ptr(), _arr(sb), len(shape), _arr(shape),
-                     DT[odt], out.ctypes.data_as(ctypes.c_void_p))
+    n = int(np.prod(shape))
+    out = np.empty(n, dtype=odt)
+    csa, csb, csh = _arr(sa), _arr(sb), _arr(shape)
+    _ranges(n, threads, lambda lo, hi: lib().orc_binary_range(
+        BINARY[op], DT[va.dtype], va.ptr(), csa, vb.ptr(), csb, len(shape), csh, DT[odt],
+        out.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(lo), ctypes.c_int64(hi)))
     return _result(out, shape)
 
 
-def scalar(op, x, s, out_dtype=None):
+def scalar(op, x, s, out_dtype=None, threads=1):
     v = View.of(x)
     odt = np.dtype(out_dtype) if out_dtype is not None else (np.dtype(np.uint8) if op in COMPARE else v.dtype)
-    out = np.empty(int(np.prod(v.shape)), dtype=odt)
-    lib().orc_scalar(BINARY[op], DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
-                     ctypes.c_double(s), DT[odt], out.ctypes.data_as(ctypes.c_void_p))
+    n = int(np.prod(v.shape))
+    out = np.empty(n, dtype=odt)
+    sh, st = _arr(v.shape), _arr(v.strides)
+    _ranges(n, threads, lambda lo, hi: lib().orc_scalar_range(
+        BINARY[op], DT[v.dtype], v.ptr(), len(v.shape), sh, st, ctypes.c_double(s), DT[odt],
+        out.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(lo), ctypes.c_int64(hi)))
     return _result(out, v.shape)
 
 
@@ -243,17 +269,23 @@ def diff(x, lag=1, differences=1):
     return np.resize(v, x.size).reshape(x.shape, order="F")
 
 
-def gauss_chain(x, p=0.5):
+def gauss_chain(x, p=0.5, threads=1):
     """x*p + exp(-(x^2)) with one rounding per R operator."""
     a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))
     out = np.empty_like(a)
-    lib().orc_gauss_chain(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
-                          ctypes.c_double(p), out.ctypes.data_as(ctypes.c_void_p))
+    if threads > 1:
+        lib_mt().orc_gauss_chain_mt(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                                    ctypes.c_double(p), out.ctypes.data_as(ctypes.c_void_p), int(threads))
+    else:
+        lib().orc_gauss_chain(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                              ctypes.c_double(p), out.ctypes.data_as(ctypes.c_void_p))
     return out.reshape(np.asarray(x).shape, order="F")
 
 
-def reduce(op, x, axes=None):
-    """Base-R reduction over `axes` (0-based list; None = all).  Returns float64."""
+def reduce(op, x, axes=None, threads=1):
+    """Base-R reduction over `axes` (0-based list; None = all).  Returns float64.
+    threads > 1 splits the outputs over threads (each output is computed by
+    the same code)."""
     v = View.of(x)
     nd = len(v.shape)
     axes = list(range(nd)) if axes is None else list(axes)
@@ -262,36 +294,116 @@ def reduce(op, x, axes=None):
         mask |= 1 << a
     kept = [v.shape[d] for d in range(nd) if d not in axes]
     out = np.empty(max(1, int(np.prod(kept))), dtype=np.float64)
-    lib().orc_reduce(REDUCE[op], DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides),
-                     ctypes.c_uint32(mask), out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+    args = (REDUCE[op], DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides), ctypes.c_uint32(mask),
+            out.ctypes.data_as(ctypes.POINTER(ctypes.c_double)))
+    if threads > 1:
+        lib_mt().orc_reduce_mt(*args, int(threads))
+    else:
+        lib().orc_reduce(*args)
     return out.reshape(kept, order="F") if kept else out[0]
 
 
-def arg_reduce(op, x, axis=None, one_based=True):
+def arg_reduce(op, x, axis=None, one_based=True, threads=1):
     v = View.of(x)
     nd = len(v.shape)
     kept = [v.shape[d] for d in range(nd) if axis is not None and d != axis]
     out = np.empty(max(1, int(np.prod(kept))), dtype=np.int64)
-    lib().orc_arg_reduce(1 if op == "argmax" else 0, DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides),
-                         -1 if axis is None else int(axis), 1 if one_based else 0,
-                         out.ctypes.data_as(_i64p))
+    args = (1 if op == "argmax" else 0, DT[v.dtype], v.ptr(), nd, _arr(v.shape), _arr(v.strides),
+            -1 if axis is None else int(axis), 1 if one_based else 0, out.ctypes.data_as(_i64p))
+    if threads > 1:
+        lib_mt().orc_arg_reduce_mt(*args, int(threads))
+    else:
+        lib().orc_arg_reduce(*args)
     return out.reshape(kept, order="F") if axis is not None else int(out[0])
 
 
-def scan(op, x, axis=None):
+def scan(op, x, axis=None, threads=1):
     v = View.of(x)
     out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
-    lib().orc_scan(1 if op == "cumprod" else 0, DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape),
-                   _arr(v.strides), -1 if axis is None else int(axis), out.ctypes.data_as(ctypes.c_void_p))
+    args = (1 if op == "cumprod" else 0, DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
+            -1 if axis is None else int(axis), out.ctypes.data_as(ctypes.c_void_p))
+    if threads > 1:
+        lib_mt().orc_scan_mt(*args, int(threads))
+    else:
+        lib().orc_scan(*args)
     return _result(out, v.shape)
 
 
-def softmax(x, axis=None):
+def softmax(x, axis=None, threads=1):
     v = View.of(x)
     out = np.empty(int(np.prod(v.shape)), dtype=v.dtype)
-    lib().orc_softmax(DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides),
-                      -1 if axis is None else int(axis), out.ctypes.data_as(ctypes.c_void_p))
+    args = (DT[v.dtype], v.ptr(), len(v.shape), _arr(v.shape), _arr(v.strides), -1 if axis is None else int(axis),
+            out.ctypes.data_as(ctypes.c_void_p))
+    if threads > 1:
+        lib_mt().orc_softmax_mt(*args, int(threads))
+    else:
+        lib().orc_softmax(*args)
     return _result(out, v.shape)
+
+
+class ChunkedStats:
+    """Base-R sum / mean / var / max / min / which.max / which.min of a
+    contiguous array too large for reduce() (which gathers a fiber into long
+    doubles first), fed in consecutive chunks and in two passes:
+
+        st = ChunkedStats(n)
+        for c in chunks: st.first(c)     # sum and the extrema
+        for c in chunks: st.second(c)    # R's mean correction and the variance
+        st.result()
+
+    Sums are long double (numpy longdouble = C long double here); the mean is
+    sum/n corrected by sum(x - m)/n as R does; the variance is two-pass around
+    the corrected mean, divisor n - 1.  Indices are 1-based, first on ties,
+    NaN never wins."""
+
+    def __init__(self, n, threads=None):
+        self.n = int(n)
+        self.threads = int(threads or default_threads())
+        self.acc1 = np.zeros(2, dtype=np.longdouble)
+        self.acc2 = np.zeros(2, dtype=np.longdouble)
+        self.zero = np.zeros(1, dtype=np.longdouble)
+        self.val = np.zeros(2, dtype=np.float64)
+        self.idx = np.full(2, -1, dtype=np.int64)
+        self.pos = 0
+        self.center = None
+
+    def first(self, chunk):
+        a = np.ascontiguousarray(chunk).reshape(-1)
+        L = lib_mt()
+        L.orc_moments_mt(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                         self.zero.ctypes.data_as(ctypes.c_void_p), self.acc1.ctypes.data_as(ctypes.c_void_p),
+                         self.threads)
+        L.orc_extrema_mt(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                         ctypes.c_int64(self.pos), self.val.ctypes.data_as(ctypes.c_void_p),
+                         self.idx.ctypes.data_as(ctypes.c_void_p), self.threads)
+        self.pos += a.size
+
+    def second(self, chunk):
+        if self.center is None:
+            self.center = np.array([self.acc1[0] / np.longdouble(self.n)], dtype=np.longdouble)
+        a = np.ascontiguousarray(chunk).reshape(-1)
+        lib_mt().orc_moments_mt(DT[a.dtype], a.ctypes.data_as(ctypes.c_void_p), ctypes.c_int64(a.size),
+                                self.center.ctypes.data_as(ctypes.c_void_p),
+                                self.acc2.ctypes.data_as(ctypes.c_void_p), self.threads)
+
+    def result(self):
+        n = np.longdouble(self.n)
+        s = self.acc1[0]
+        m = self.center[0]
+        t, q = self.acc2[0], self.acc2[1]
+        mean = m + t / n
+        var = (q - t * t / n) / (n - 1) if self.n > 1 else np.longdouble(np.nan)
+        return {"sum": float(s), "mean": float(mean), "var": float(var), "max": float(self.val[0]),
+                "min": float(self.val[1]), "which_max": int(self.idx[0]) + 1, "which_min": int(self.idx[1]) + 1}
+
+
+def full_stats(x, threads=None):
+    """ChunkedStats over one array (any size; column-major element order)."""
+    a = np.ascontiguousarray(np.asarray(x).reshape(-1, order="F"))
+    st = ChunkedStats(a.size, threads)
+    st.first(a)
+    st.second(a)
+    return st.result()
 
 
 def sum_var(x):
