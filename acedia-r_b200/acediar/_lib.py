@@ -12,10 +12,11 @@ LIB_PATH = os.path.join(PKG, "lib", "libacediar_b200.so")
 
 MAX_DIMS = 8
 
-FLOAT32, FLOAT64, INT32, INT64, BOOL = 0, 1, 2, 3, 4
-DTYPE_CODES = {"float": FLOAT32, "double": FLOAT64, "int32": INT32, "int64": INT64, "bool": BOOL}
+FLOAT32, FLOAT64, INT32, INT64, BOOL, FLOAT16, INT8 = 0, 1, 2, 3, 4, 5, 6
+DTYPE_CODES = {"float": FLOAT32, "double": FLOAT64, "int32": INT32, "int64": INT64, "bool": BOOL,
+               "float16": FLOAT16, "int8": INT8}
 DTYPE_NAMES = {v: k for k, v in DTYPE_CODES.items()}
-DTYPE_SIZES = {FLOAT32: 4, FLOAT64: 8, INT32: 4, INT64: 8, BOOL: 1}
+DTYPE_SIZES = {FLOAT32: 4, FLOAT64: 8, INT32: 4, INT64: 8, BOOL: 1, FLOAT16: 2, INT8: 1}
 
 UNARY = {n: i for i, n in enumerate(
     ["exp", "log", "sqrt", "abs", "floor", "ceil", "round", "erf", "tanh", "sigmoid", "relu", "sin", "cos",
@@ -105,6 +106,8 @@ def _bind(lib):
         "acd_stats_partial": ([vp, vp, dp, vp], i32),
         "acd_argmax_keys": ([vp, vp, dp, i32, i64, vp], i32),
         "acd_argmax_keys_decode": ([vp, dp, vp, i32, vp], i32),
+        "acd_shard_exchange_init": ([vp, vp, i64, i32, vp], i32),
+        "acd_shard_finish": ([vp, vp, i64, i32, dp, vp, i32, vp], i32),
         "acd_fused_stats_keys": ([vp, dp, dp, f64, vp, vp, i64, vp], i32),
         "acd_permute_fused_stats_keys": ([vp, dp, dp, dp, f64, vp, vp, i64, vp], i32),
         "acd_selftest_fastdiv": ([u32, u32, P(u32)], i32),

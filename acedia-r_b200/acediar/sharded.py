@@ -16,6 +16,12 @@ other ranks:
 The statistics row and the keys can come from the pass that writes the
 elementwise chain (chain_stats_keys; permute_chain_stats_keys adds the
 contiguous copy in front), so z is written once and not re-read.
+
+Both exchanges travel in one int64 MAX all-reduce over an exchange buffer
+(exchange_buffer, shard_finish): the keys, then one row of six float64 bit
+patterns per rank, where every rank leaves the other ranks' rows at
+INT64_MIN (the bit pattern of -0.0 and the smallest int64), so MAX copies
+each rank's row to all ranks unchanged.
 There is no peer-memory access and no multicast: the exchanged bytes are a few
 doubles and one key per output (1 MiB at 256 x 512).
 """
@@ -75,6 +81,27 @@ def pack_keys_np(values, index):
     ordered = np.where(v & 0x80000000, (~v) & 0xFFFFFFFF, v | 0x80000000)
     u = (ordered << np.uint64(32)) | (np.uint64(0xFFFFFFFF) - np.asarray(index, dtype=np.uint64))
     return (u ^ np.uint64(0x8000000000000000)).view(np.int64)
+
+
+INT64_MIN = np.iinfo(np.int64).min
+
+
+def pack_exchange_np(keys, row, rank, world):
+    """Host reference of one rank's exchange buffer: its keys, its statistics
+    row as float64 bit patterns in slot `rank`, INT64_MIN in the others."""
+    buf = np.full(len(keys) + STATS_WIDTH * world, INT64_MIN, dtype=np.int64)
+    buf[:len(keys)] = keys
+    buf[len(keys) + STATS_WIDTH * rank:len(keys) + STATS_WIDTH * (rank + 1)] = \
+        np.asarray(row, dtype=np.float64).view(np.int64)
+    return buf
+
+
+def finish_exchange_np(buf, nkeys, world, one_based=True):
+    """Host reference of acd_shard_finish on an all-reduced buffer: the rows
+    (merged in rank order as merge_stats_torch does) and the decoded keys."""
+    rows = np.asarray(buf[nkeys:nkeys + STATS_WIDTH * world], dtype=np.int64).view(np.float64).reshape(world, -1)
+    tot, var = merge_stats_torch(torch.from_numpy(rows.copy()))
+    return float(tot), float(var), decode_keys_np(buf[:nkeys], one_based)
 
 
 def decode_keys_np(keys, one_based=True):
@@ -140,6 +167,34 @@ def decode_keys(keys, shape, one_based=True, dtype="int32"):
     L.check(L.lib().acd_argmax_keys_decode(context(), ctypes.byref(out.desc()), ctypes.c_void_p(keys.data_ptr()),
                                            1 if one_based else 0, _stream()), "argmax_keys_decode")
     return out
+
+
+def exchange_buffer(nkeys, world, device):
+    """The int64 exchange buffer (keys, then one statistics row per rank),
+    with every row at INT64_MIN."""
+    buf = torch.empty(nkeys + STATS_WIDTH * world, dtype=torch.int64, device=device)
+    L.check(L.lib().acd_shard_exchange_init(context(), ctypes.c_void_p(buf.data_ptr()), int(nkeys), int(world),
+                                            _stream()), "shard_exchange_init")
+    return buf
+
+
+def row_slot(buf, nkeys, rank):
+    """Device address of `rank`'s statistics row inside the exchange buffer."""
+    return ctypes.c_void_p(buf.data_ptr() + 8 * (nkeys + STATS_WIDTH * rank))
+
+
+def shard_finish(buf, nkeys, world, shape, one_based=True, dtype="int32", out=None, sum_var=None):
+    """After the MAX all-reduce of `buf`: argmax indices of shape `shape`,
+    and a float64[2] device tensor (sum, var); the rows are reset for the
+    next exchange."""
+    if out is None:
+        out = _alloc(tuple(shape), dtype, buf.device)
+    if sum_var is None:
+        sum_var = torch.empty(2, dtype=torch.float64, device=buf.device)
+    L.check(L.lib().acd_shard_finish(context(), ctypes.c_void_p(buf.data_ptr()), int(nkeys), int(world),
+                                     ctypes.byref(out.desc()), ctypes.c_void_p(sum_var.data_ptr()),
+                                     1 if one_based else 0, _stream()), "shard_finish")
+    return out, sum_var
 
 
 def shard_bounds(n, rank, world):

@@ -25,10 +25,12 @@ import torch
 from . import _lib as L
 
 _TORCH = {"float": torch.float32, "double": torch.float64, "int32": torch.int32, "int64": torch.int64,
-          "bool": torch.uint8}
-_NUMPY = {"float": np.float32, "double": np.float64, "int32": np.int32, "int64": np.int64, "bool": np.bool_}
+          "bool": torch.uint8, "float16": torch.float16, "int8": torch.int8}
+_NUMPY = {"float": np.float32, "double": np.float64, "int32": np.int32, "int64": np.int64, "bool": np.bool_,
+          "float16": np.float16, "int8": np.int8}
 _ALIASES = {"float32": "float", "float64": "double", "float": "float", "double": "double", "int32": "int32",
-            "int64": "int64", "bool": "bool", "logical": "bool"}
+            "int64": "int64", "bool": "bool", "logical": "bool", "float16": "float16", "half": "float16",
+            "int8": "int8"}
 
 _ctx = {}
 
@@ -270,7 +272,18 @@ def compare(op, a, b, dtype_out=None):
 
 
 def exp(x): return _unary("exp", x)
-def log(x): return _unary("log", x)
+
+
+def log(x, base=np.e):
+    """log.gpuTensor (R/gpuTensor.R:873-883) over tensor_log_unified
+    (src/TensorMath.cpp:167-174): natural logarithm only, and an input with a
+    value <= 0 is an error (NaN is not).  The check runs on the device (one
+    comparison and count) where the reference copies the tensor to the host."""
+    if base != np.e:
+        raise ValueError("Only natural logarithm (base e) is currently supported")
+    if x.dtype in ("float", "double") and tensor_count(_arith("le", x, 0.0)).as_array().reshape(-1)[0] > 0:
+        raise ValueError("log() domain error: input contains non-positive values")
+    return _unary("log", x)
 def sqrt(x): return _unary("sqrt", x)
 def abs(x): return _unary("abs", x)
 def floor(x): return _unary("floor", x)
@@ -666,7 +679,7 @@ def rnorm(x, mean=0.0, sd=1.0):
 
 _DTYPE_ALIASES = {"float32": "float", "float": "float", "float64": "double", "double": "double",
                   "int32": "int32", "int": "int32", "int64": "int64", "long": "int64", "bool": "bool",
-                  "logical": "bool"}
+                  "logical": "bool", "float16": "float16", "half": "float16", "int8": "int8"}
 
 
 def to_dtype(x, target_dtype):
@@ -720,10 +733,12 @@ def _reduce(op, x, axis=None, keep_dims=False, out_dtype=None):
     if out_dtype is None:
         if op == "count":
             out_dtype = "int32"
-        elif x.dtype == "bool":
-            out_dtype = "int32"
+        elif x.dtype in ("bool", "int8"):
+            out_dtype = "double" if op == "mean" else "int32"
         elif x.dtype in ("int32", "int64") and op in ("mean", "var", "prod"):
             out_dtype = "double"
+        elif x.dtype == "float16":
+            out_dtype = "float"  # the reference's float16 sum returns float (src/TensorReduction.cpp:12)
         else:
             out_dtype = x.dtype
     out = _alloc(tuple(oshape), out_dtype, x.device)
@@ -769,8 +784,8 @@ def all(x, axis=None):
 
 def _r_reduce(op):
     def f(x, axis=None, keep_dims=False):
-        t = _reduce(op, x, axis, keep_dims, out_dtype="double" if axis is None and x.dtype in ("float", "double")
-                    else None)
+        t = _reduce(op, x, axis, keep_dims,
+                    out_dtype="double" if axis is None and x.dtype in ("float", "double", "float16") else None)
         return _scalar_result(t) if axis is None else t
     f.__name__ = op
     f.__doc__ = "R's %s.gpuTensor: a number without axis, a gpuTensor with axis (1-based)." % op

@@ -75,7 +75,8 @@ def build(force=False, jobs=None, verbose=False):
             for log in ex.map(lambda so: _compile(nvcc, so[0], so[1], verbose), todo):
                 logs.append(log)
     if todo or not os.path.exists(LIB):
-        cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB] + objs + ["-lcudart"]
+        # cuBLAS (contraction launchers only) is opened with dlopen at first use: -ldl, no -lcublas
+        cmd = [nvcc, "-shared", "-gencode", "arch=compute_100a,code=sm_100a", "-o", LIB] + objs + ["-lcudart", "-ldl"]
         r = subprocess.run(cmd, capture_output=True, text=True)
         if r.returncode != 0:
             raise RuntimeError("link failed:\n%s%s" % (r.stdout, r.stderr))

@@ -3,12 +3,14 @@
 // reporting and the context layout.
 #pragma once
 
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include <cmath>
 #include <cstring>
 #include <string>
+#include <type_traits>
 
 #include "../../include/acd.h"
 
@@ -43,10 +45,16 @@ inline size_t dtype_size(int32_t dt) {
     case ACD_INT32: return 4;
     case ACD_INT64: return 8;
     case ACD_BOOL: return 1;
+    case ACD_FLOAT16: return 2;
+    case ACD_INT8: return 1;
     default: return 0;
   }
 }
 inline bool is_float(int32_t dt) { return dt == ACD_FLOAT32 || dt == ACD_FLOAT64; }
+
+// Real (non-integer) element types: float, double and IEEE binary16.
+template <typename T>
+struct is_real : std::integral_constant<bool, std::is_floating_point<T>::value || std::is_same<T, __half>::value> {};
 
 // ---------------------------------------------------------------------------
 // context

@@ -500,6 +500,12 @@ static acd_status binary_to(acd_ctx *ctx, int op, const acd_desc *out, const acd
       ACD_B(ACD_GT) ACD_B(ACD_LT) ACD_B(ACD_EQ) ACD_B(ACD_NE) ACD_B(ACD_GE) ACD_B(ACD_LE)
       default: break;
     }
+  } else if constexpr (std::is_same<T, __half>::value) {
+    switch (op) {
+      ACD_B(ACD_ADD) ACD_B(ACD_SUB) ACD_B(ACD_MUL) ACD_B(ACD_DIV) ACD_B(ACD_MAX) ACD_B(ACD_MIN)
+      ACD_B(ACD_GT) ACD_B(ACD_LT) ACD_B(ACD_EQ) ACD_B(ACD_NE) ACD_B(ACD_GE) ACD_B(ACD_LE)
+      default: break;
+    }
   } else {
     switch (op) {
       ACD_B(ACD_ADD) ACD_B(ACD_SUB) ACD_B(ACD_MUL) ACD_B(ACD_MAX) ACD_B(ACD_MIN)
@@ -514,7 +520,11 @@ static acd_status binary_to(acd_ctx *ctx, int op, const acd_desc *out, const acd
 template <typename T, typename O>
 static acd_status scalar_to(acd_ctx *ctx, int op, const acd_desc *out, const acd_desc *in, double sv,
                             cudaStream_t s) {
-  const T ts = (T)sv;
+  T ts;
+  if constexpr (std::is_same<T, __half>::value)
+    ts = __double2half(sv);  // the scalar rounds once to the tensor dtype
+  else
+    ts = (T)sv;
   const int64_t *st = in->stride;
 #define ACD_S(OPC)                                                                            \
   case OPC:                                                                                   \
@@ -529,6 +539,13 @@ static acd_status scalar_to(acd_ctx *ctx, int op, const acd_desc *out, const acd
     if (op == ACD_POW && sv == 2.0) return launch_map(ctx, SquareScalarF<T>{}, out, in, st, nullptr, nullptr, s);
     switch (op) {
       ACD_S(ACD_ADD) ACD_S(ACD_SUB) ACD_S(ACD_MUL) ACD_S(ACD_DIV) ACD_S(ACD_MAX) ACD_S(ACD_MIN) ACD_S(ACD_POW)
+      ACD_S(ACD_GT) ACD_S(ACD_LT) ACD_S(ACD_EQ) ACD_S(ACD_NE) ACD_S(ACD_GE) ACD_S(ACD_LE)
+      ACD_S(ACD_RSUB) ACD_S(ACD_RDIV)
+      default: break;
+    }
+  } else if constexpr (std::is_same<T, __half>::value) {
+    switch (op) {
+      ACD_S(ACD_ADD) ACD_S(ACD_SUB) ACD_S(ACD_MUL) ACD_S(ACD_DIV) ACD_S(ACD_MAX) ACD_S(ACD_MIN)
       ACD_S(ACD_GT) ACD_S(ACD_LT) ACD_S(ACD_EQ) ACD_S(ACD_NE) ACD_S(ACD_GE) ACD_S(ACD_LE)
       ACD_S(ACD_RSUB) ACD_S(ACD_RDIV)
       default: break;
@@ -666,6 +683,8 @@ static acd_status convert_from(acd_ctx *ctx, const acd_desc *out, const acd_desc
     case ACD_INT32: return launch_map(ctx, ConvertF<From, int32_t>{}, out, in, st, nullptr, nullptr, s);
     case ACD_INT64: return launch_map(ctx, ConvertF<From, int64_t>{}, out, in, st, nullptr, nullptr, s);
     case ACD_BOOL: return launch_map(ctx, ConvertF<From, uint8_t>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_FLOAT16: return launch_map(ctx, ConvertF<From, __half>{}, out, in, st, nullptr, nullptr, s);
+    case ACD_INT8: return launch_map(ctx, ConvertF<From, int8_t>{}, out, in, st, nullptr, nullptr, s);
     default: return fail(ACD_ERR_DTYPE, "acd_convert: target dtype %d not supported", out->dtype);
   }
 }
@@ -691,6 +710,8 @@ acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, ac
     case ACD_INT32: st = convert_from<int32_t>(ctx, out, in, s); break;
     case ACD_INT64: st = convert_from<int64_t>(ctx, out, in, s); break;
     case ACD_BOOL: st = convert_from<uint8_t>(ctx, out, in, s); break;
+    case ACD_FLOAT16: st = convert_from<__half>(ctx, out, in, s); break;
+    case ACD_INT8: st = convert_from<int8_t>(ctx, out, in, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_convert: source dtype %d not supported", in->dtype);
   }
   if (st != ACD_OK) return st;
@@ -711,6 +732,8 @@ acd_status acd_fill(acd_ctx *ctx, const acd_desc *out, double value, acd_stream 
     case ACD_INT32: st = fill_t<int32_t>(ctx, out, value, s); break;
     case ACD_INT64: st = fill_t<int64_t>(ctx, out, value, s); break;
     case ACD_BOOL: st = fill_t<uint8_t>(ctx, out, value, s); break;
+    case ACD_FLOAT16: st = fill_t<__half>(ctx, out, value, s); break;
+    case ACD_INT8: st = fill_t<int8_t>(ctx, out, value, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_fill: dtype %d not supported", out->dtype);
   }
   if (st != ACD_OK) return st;
@@ -733,6 +756,8 @@ acd_status acd_mask_fill(acd_ctx *ctx, const acd_desc *x, const acd_desc *mask, 
     case ACD_INT32: st = mask_fill_t<int32_t>(ctx, x, mask, value, s); break;
     case ACD_INT64: st = mask_fill_t<int64_t>(ctx, x, mask, value, s); break;
     case ACD_BOOL: st = mask_fill_t<uint8_t>(ctx, x, mask, value, s); break;
+    case ACD_FLOAT16: st = mask_fill_t<__half>(ctx, x, mask, value, s); break;
+    case ACD_INT8: st = mask_fill_t<int8_t>(ctx, x, mask, value, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_mask_fill: dtype %d not supported", x->dtype);
   }
   if (st != ACD_OK) return st;
@@ -754,6 +779,8 @@ acd_status acd_unary(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_de
     case ACD_FLOAT64: st = unary_t<double>(ctx, op, out, in, s); break;
     case ACD_INT32: st = unary_t<int32_t>(ctx, op, out, in, s); break;
     case ACD_INT64: st = unary_t<int64_t>(ctx, op, out, in, s); break;
+    case ACD_FLOAT16: st = unary_t<__half>(ctx, op, out, in, s); break;
+    case ACD_INT8: st = unary_t<int8_t>(ctx, op, out, in, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_unary: dtype %d not supported", in->dtype);
   }
   if (st != ACD_OK) return st;
@@ -803,6 +830,14 @@ acd_status acd_binary(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
       st = to_bool ? binary_to<int64_t, uint8_t>(ctx, op, out, a, sa, b, sb, s)
                    : binary_to<int64_t, int64_t>(ctx, op, out, a, sa, b, sb, s);
       break;
+    case ACD_FLOAT16:
+      st = to_bool ? binary_to<__half, uint8_t>(ctx, op, out, a, sa, b, sb, s)
+                   : binary_to<__half, __half>(ctx, op, out, a, sa, b, sb, s);
+      break;
+    case ACD_INT8:
+      st = to_bool ? binary_to<int8_t, uint8_t>(ctx, op, out, a, sa, b, sb, s)
+                   : binary_to<int8_t, int8_t>(ctx, op, out, a, sa, b, sb, s);
+      break;
     default: return fail(ACD_ERR_DTYPE, "acd_binary: dtype %d not supported", a->dtype);
   }
   if (st != ACD_OK) return st;
@@ -838,6 +873,14 @@ acd_status acd_scalar(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
     case ACD_INT64:
       st = to_bool ? scalar_to<int64_t, uint8_t>(ctx, op, out, in, sv, s)
                    : scalar_to<int64_t, int64_t>(ctx, op, out, in, sv, s);
+      break;
+    case ACD_FLOAT16:
+      st = to_bool ? scalar_to<__half, uint8_t>(ctx, op, out, in, sv, s)
+                   : scalar_to<__half, __half>(ctx, op, out, in, sv, s);
+      break;
+    case ACD_INT8:
+      st = to_bool ? scalar_to<int8_t, uint8_t>(ctx, op, out, in, sv, s)
+                   : scalar_to<int8_t, int8_t>(ctx, op, out, in, sv, s);
       break;
     default: return fail(ACD_ERR_DTYPE, "acd_scalar: dtype %d not supported", in->dtype);
   }
@@ -898,6 +941,7 @@ acd_status acd_copy(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_s
   acd_status st;
   switch (dtype_size(in->dtype)) {
     case 1: st = copy_sized<uint8_t, 64>(ctx, out, in, s); break;
+    case 2: st = copy_sized<uint16_t, 64>(ctx, out, in, s); break;
     case 4: st = copy_sized<uint32_t, 64>(ctx, out, in, s); break;
     case 8: st = copy_sized<uint64_t, 32>(ctx, out, in, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_copy: bad dtype");

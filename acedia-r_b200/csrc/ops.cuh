@@ -41,14 +41,17 @@ __device__ __forceinline__ float m_rint(float x) { return rintf(x); }
 __device__ __forceinline__ double m_rint(double x) { return rint(x); }
 __device__ __forceinline__ float m_abs(float x) { return fabsf(x); }
 __device__ __forceinline__ double m_abs(double x) { return fabs(x); }
+__device__ __forceinline__ int8_t m_abs(int8_t x) { return (int8_t)(x < 0 ? -x : x); }
 __device__ __forceinline__ int32_t m_abs(int32_t x) { return x < 0 ? -x : x; }
 __device__ __forceinline__ int64_t m_abs(int64_t x) { return x < 0 ? -x : x; }
 __device__ __forceinline__ float m_max(float a, float b) { return fmaxf(a, b); }
 __device__ __forceinline__ double m_max(double a, double b) { return fmax(a, b); }
+__device__ __forceinline__ int8_t m_max(int8_t a, int8_t b) { return a > b ? a : b; }
 __device__ __forceinline__ int32_t m_max(int32_t a, int32_t b) { return a > b ? a : b; }
 __device__ __forceinline__ int64_t m_max(int64_t a, int64_t b) { return a > b ? a : b; }
 __device__ __forceinline__ float m_min(float a, float b) { return fminf(a, b); }
 __device__ __forceinline__ double m_min(double a, double b) { return fmin(a, b); }
+__device__ __forceinline__ int8_t m_min(int8_t a, int8_t b) { return a < b ? a : b; }
 __device__ __forceinline__ int32_t m_min(int32_t a, int32_t b) { return a < b ? a : b; }
 __device__ __forceinline__ int64_t m_min(int64_t a, int64_t b) { return a < b ? a : b; }
 // float pow is evaluated in double and rounded once (CUDA's double pow is
@@ -56,9 +59,53 @@ __device__ __forceinline__ int64_t m_min(int64_t a, int64_t b) { return a < b ? 
 __device__ __forceinline__ float m_pow(float a, float b) { return (float)pow((double)a, (double)b); }
 __device__ __forceinline__ double m_pow(double a, double b) { return pow(a, b); }
 
+// A comparison result (1 or 0) in the output dtype.
+template <typename O>
+__device__ __forceinline__ O flag_as(bool c) {
+  if constexpr (std::is_same<O, __half>::value)
+    return __float2half_rn(c ? 1.0f : 0.0f);
+  else
+    return O(c ? 1 : 0);
+}
+
+// IEEE binary16 (FLOAT16 tensors): each operation is evaluated in float32 on
+// the exact half operands and rounded once to half.  For + - * / and the
+// square this equals the correctly rounded binary16 result (float32 carries
+// 24 bits >= 2*11 + 2, so the double rounding is innocuous), i.e. the
+// reference's half operator arithmetic (src/kernels/tensor_kernels.cuh:10-25
+// applied to half).
+template <int OP>
+__device__ __forceinline__ __half half_unary(__half x) {
+  const float f = __half2float(x);
+  if constexpr (OP == ACD_ABS) return __float2half_rn(fabsf(f));
+  else if constexpr (OP == ACD_NEG) return __float2half_rn(-f);
+  else if constexpr (OP == ACD_SQUARE) return __float2half_rn(f * f);
+  else return x;  // ACD_COPY
+}
+
+template <int OP, typename O>
+__device__ __forceinline__ O half_binary(__half a, __half b) {
+  const float x = __half2float(a), y = __half2float(b);
+  if constexpr (OP == ACD_GT) return flag_as<O>(x > y);
+  else if constexpr (OP == ACD_LT) return flag_as<O>(x < y);
+  else if constexpr (OP == ACD_EQ) return flag_as<O>(x == y);
+  else if constexpr (OP == ACD_NE) return flag_as<O>(x != y);
+  else if constexpr (OP == ACD_GE) return flag_as<O>(x >= y);
+  else if constexpr (OP == ACD_LE) return flag_as<O>(x <= y);
+  else if constexpr (OP == ACD_ADD) return __float2half_rn(x + y);
+  else if constexpr (OP == ACD_SUB) return __float2half_rn(x - y);
+  else if constexpr (OP == ACD_MUL) return __float2half_rn(x * y);
+  else if constexpr (OP == ACD_DIV) return __float2half_rn(x / y);
+  else if constexpr (OP == ACD_MAX) return __float2half_rn(fmaxf(x, y));
+  else if constexpr (OP == ACD_MIN) return __float2half_rn(fminf(x, y));
+  else if constexpr (OP == ACD_RSUB) return __float2half_rn(y - x);
+  else return __float2half_rn(y / x);  // ACD_RDIV
+}
+
 template <int OP, typename T>
 __device__ __forceinline__ T unary_apply(T x) {
-  if constexpr (OP == ACD_EXP) return m_exp(x);
+  if constexpr (std::is_same<T, __half>::value) return half_unary<OP>(x);
+  else if constexpr (OP == ACD_EXP) return m_exp(x);
   else if constexpr (OP == ACD_LOG) return m_log(x);
   else if constexpr (OP == ACD_SQRT) return m_sqrt(x);
   else if constexpr (OP == ACD_ABS) return m_abs(x);
@@ -78,14 +125,15 @@ __device__ __forceinline__ T unary_apply(T x) {
   else if constexpr (OP == ACD_RELU) return m_max(x, T(0));
   else if constexpr (OP == ACD_SIN) return m_sin(x);
   else if constexpr (OP == ACD_COS) return m_cos(x);
-  else if constexpr (OP == ACD_NEG) return -x;
-  else if constexpr (OP == ACD_SQUARE) return x * x;
+  else if constexpr (OP == ACD_NEG) return T(-x);
+  else if constexpr (OP == ACD_SQUARE) return T(x * x);
   else return x;  // ACD_COPY
 }
 
 template <int OP, typename T, typename O>
 __device__ __forceinline__ O binary_apply(T a, T b) {
-  if constexpr (OP == ACD_ADD) return O(a + b);
+  if constexpr (std::is_same<T, __half>::value) return half_binary<OP, O>(a, b);
+  else if constexpr (OP == ACD_ADD) return O(a + b);
   else if constexpr (OP == ACD_SUB) return O(a - b);
   else if constexpr (OP == ACD_MUL) return O(a * b);
   else if constexpr (OP == ACD_DIV) return O(a / b);
@@ -143,10 +191,31 @@ struct SquareScalarF {
 // NA (INT32_MIN for int32, INT64_MIN for int64); an NA integer becomes NaN in
 // a floating type; float <-> double and int64 -> float round to nearest;
 // bool stores x != 0 (bool has no NA, so NaN and NA integers become 1).
+// The two narrow types R lacks follow the reference's device casts:
+// float16 is reached by one rounding to nearest from the exact source value
+// (NA integers become NaN) and converts onward exactly through float32;
+// int8 has no NA: from a floating value it truncates toward zero and
+// saturates to [-128, 127] with NaN -> 0 (the device's float-to-int8 cast),
+// from a wider integer it keeps the low 8 bits, and it widens exactly.
 template <typename From, typename To>
 __host__ __device__ __forceinline__ To convert_value(From x) {
   if constexpr (std::is_same<From, To>::value) {
     return x;
+  } else if constexpr (std::is_same<From, __half>::value) {
+    return convert_value<float, To>(__half2float(x));  // half -> float is exact
+  } else if constexpr (std::is_same<To, __half>::value) {
+    // double holds every float32, int32 and int8 value exactly (int64 beyond
+    // 2^53 overflows half either way)
+    return __double2half(convert_value<From, double>(x));
+  } else if constexpr (std::is_same<To, int8_t>::value) {
+    if constexpr (std::is_floating_point<From>::value) {
+      if (x != x) return 0;
+      if (x <= (From)-128) return -128;
+      if (x >= (From)127) return 127;
+      return (int8_t)x;
+    } else {
+      return (int8_t)x;
+    }
   } else if constexpr (std::is_same<To, uint8_t>::value) {
     return (uint8_t)(x != From(0));
   } else if constexpr (std::is_floating_point<To>::value) {

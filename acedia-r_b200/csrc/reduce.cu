@@ -799,6 +799,17 @@ static acd_status reduce_t(acd_ctx *ctx, int op, const Plan &p, const OutSpec &o
   return fail(ACD_ERR_UNSUPPORTED, "reduction op %d not supported for this dtype", op);
 }
 
+// float16 tensors: sum, mean and count (accumulated in float64 / int64)
+static acd_status reduce_half(acd_ctx *ctx, int op, const Plan &p, const OutSpec &os, cudaStream_t s) {
+  switch (op) {
+    case ACD_RED_SUM:
+    case ACD_RED_MEAN: return run_plan<SumAcc<__half>, __half>(ctx, p, os, s);
+    case ACD_RED_COUNT: return run_plan<CountAcc<__half>, __half>(ctx, p, os, s);
+    default: break;
+  }
+  return fail(ACD_ERR_UNSUPPORTED, "reduction op %d not supported for float16 (sum, mean and count are)", op);
+}
+
 template <typename T>
 static acd_status arg_t(acd_ctx *ctx, int op, const Plan &p, const OutSpec &os, cudaStream_t s) {
   if (op == ACD_ARGMAX) return run_plan<ArgAcc<T, true>, T>(ctx, p, os, s);
@@ -810,7 +821,8 @@ static acd_status check_out_count(const acd_desc *out, int64_t want, const char 
     return fail(ACD_ERR_SHAPE, "%s: output has %lld elements, expected %lld", what, (long long)desc_numel(out),
                 (long long)want);
   if (!desc_is_contiguous(out)) return fail(ACD_ERR_UNSUPPORTED, "%s: output must be contiguous", what);
-  if (out->dtype == ACD_BOOL) return fail(ACD_ERR_DTYPE, "%s: bool output not supported", what);
+  if (out->dtype != ACD_FLOAT32 && out->dtype != ACD_FLOAT64 && out->dtype != ACD_INT32 && out->dtype != ACD_INT64)
+    return fail(ACD_ERR_DTYPE, "%s: output dtype must be float, double, int32 or int64", what);
   return ACD_OK;
 }
 
@@ -832,6 +844,52 @@ __global__ void __launch_bounds__(256) k_keys_decode(void *out, int32_t dt, cons
     }
     store_i(out, dt, i, idx);
   }
+}
+
+// The exchange buffer of the sharded strided-views step: int64
+// buf[nkeys + 6 * world], the argmax keys followed by one statistics row
+// (n, K, s1_hi, s2_hi, s1_lo, s2_lo as float64 bit patterns) per rank.  Each
+// rank writes its keys and its own row and leaves the other ranks' rows at
+// INT64_MIN, the bit pattern of -0.0 and the smallest int64, so one int64 MAX
+// all-reduce both picks every key's winner and hands each rank's row to all
+// ranks unchanged.  k_shard_finish then decodes the keys, merges the rows in
+// rank order (Chan's shifted-moment merge, the same float64 arithmetic as
+// the host merge in acediar/sharded.py) and puts INT64_MIN back into every
+// row for the next exchange.
+__global__ void __launch_bounds__(256) k_shard_finish(void *out, int32_t dt, long long *__restrict__ buf, int64_t nkeys,
+                                                      int32_t world, double *__restrict__ sum_var, int32_t one_based) {
+  for (int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; i < nkeys; i += (int64_t)gridDim.x * blockDim.x) {
+    const long long k = buf[i];
+    long long idx = -1;
+    if (k != LLONG_MIN) {
+      const uint64_t u = (uint64_t)k ^ 0x8000000000000000ull;
+      idx = (long long)(0xFFFFFFFFull - (u & 0xFFFFFFFFull)) + one_based;
+    }
+    store_i(out, dt, i, idx);
+  }
+  if (blockIdx.x == 0 && threadIdx.x == 0) {
+    long long *rows = buf + nkeys;
+    const double k0 = __longlong_as_double(rows[1]);
+    double s1 = 0.0, s2 = 0.0, nt = 0.0;
+    for (int r = 0; r < world; ++r) {
+      const long long *row = rows + 6 * r;
+      const double n = __longlong_as_double(row[0]), k = __longlong_as_double(row[1]);
+      const double a = __longlong_as_double(row[2]) + __longlong_as_double(row[4]);
+      const double b = __longlong_as_double(row[3]) + __longlong_as_double(row[5]);
+      const double d = k - k0;
+      s1 += a + n * d;
+      s2 += b + 2.0 * d * a + n * d * d;
+      nt += n;
+    }
+    sum_var[0] = nt * k0 + s1;
+    sum_var[1] = nt > 1.0 ? (s2 - s1 * (s1 / nt)) / (nt - 1.0) : (double)NAN;
+    for (int64_t j = 0; j < 6 * (int64_t)world; ++j) rows[j] = LLONG_MIN;
+  }
+}
+
+__global__ void k_shard_rows_init(long long *rows, int64_t n) {
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
+    rows[j] = LLONG_MIN;
 }
 
 template <typename T>
@@ -878,6 +936,8 @@ acd_status acd_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_d
     case ACD_INT32: st = reduce_t<int32_t>(ctx, op, p, os, s); break;
     case ACD_INT64: st = reduce_t<int64_t>(ctx, op, p, os, s); break;
     case ACD_BOOL: st = reduce_t<uint8_t>(ctx, op, p, os, s); break;
+    case ACD_INT8: st = reduce_t<int8_t>(ctx, op, p, os, s); break;
+    case ACD_FLOAT16: st = reduce_half(ctx, op, p, os, s); break;
     default: return fail(ACD_ERR_DTYPE, "acd_reduce: bad dtype");
   }
   if (st != ACD_OK) return st;
@@ -1016,6 +1076,32 @@ acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const
   const int grid = grid_for(ctx, n, 256, 4);
   k_keys_decode<<<grid, 256, 0, s>>>(desc_ptr(out_index), out_index->dtype, reinterpret_cast<const long long *>(keys),
                                      n, one_based ? 1 : 0);
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_shard_exchange_init(acd_ctx *ctx, int64_t *buf, int64_t nkeys, int32_t world, acd_stream stream) {
+  if (!ctx || !buf || nkeys < 0 || world < 1) return fail(ACD_ERR_INVALID, "acd_shard_exchange_init: bad argument");
+  DeviceGuard g(ctx->device);
+  k_shard_rows_init<<<1, 64, 0, static_cast<cudaStream_t>(stream)>>>(reinterpret_cast<long long *>(buf + nkeys),
+                                                                    6 * (int64_t)world);
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_shard_finish(acd_ctx *ctx, int64_t *buf, int64_t nkeys, int32_t world, const acd_desc *out_index,
+                            double *sum_var, int32_t one_based, acd_stream stream) {
+  if (!ctx || !buf || !sum_var || nkeys < 0 || world < 1) return fail(ACD_ERR_INVALID, "acd_shard_finish: bad argument");
+  ACD_TRY(check_desc(out_index, "out_index"));
+  if (!desc_is_contiguous(out_index) || desc_numel(out_index) != nkeys)
+    return fail(ACD_ERR_SHAPE, "acd_shard_finish: out_index must be contiguous with nkeys elements");
+  if (out_index->dtype != ACD_INT32 && out_index->dtype != ACD_INT64)
+    return fail(ACD_ERR_DTYPE, "acd_shard_finish: int32 or int64 output required");
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = grid_for(ctx, nkeys > 0 ? nkeys : 1, 256, 4);
+  k_shard_finish<<<grid, 256, 0, s>>>(desc_ptr(out_index), out_index->dtype, reinterpret_cast<long long *>(buf), nkeys,
+                                      world, sum_var, one_based ? 1 : 0);
   ACD_CUDA(cudaGetLastError());
   return ACD_OK;
 }

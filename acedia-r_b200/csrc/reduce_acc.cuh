@@ -112,6 +112,22 @@ struct SumAcc<double> {
   }
 };
 
+// float16: every half value is exact in float64, so the sum is a float64
+// accumulation of the exact values (the reference's tensor_sum_float16 is a
+// placeholder returning 0, src/kernels/tensor_ops.cu:701-705).
+template <>
+struct SumAcc<__half> {
+  static constexpr bool kShift = false;
+  double s;
+  __device__ __forceinline__ void init() { s = 0.0; }
+  __device__ __forceinline__ void set_shift(__half) {}
+  __device__ __forceinline__ void add(__half x, int64_t) { s += (double)__half2float(x); }
+  __device__ __forceinline__ void merge(const SumAcc &o) { s += o.s; }
+  __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const {
+    store_f(os.out, os.dt, oi, os.op == ACD_RED_MEAN ? s / (double)os.n : s);
+  }
+};
+
 template <typename T>
 struct SumAcc<T, std::enable_if_t<std::is_integral<T>::value>> {
   static constexpr bool kShift = false;
@@ -134,7 +150,12 @@ struct CountAcc {
   long long c;
   __device__ __forceinline__ void init() { c = 0; }
   __device__ __forceinline__ void set_shift(T) {}
-  __device__ __forceinline__ void add(T x, int64_t) { c += (x != T(0)) ? 1 : 0; }
+  __device__ __forceinline__ void add(T x, int64_t) {
+    if constexpr (std::is_same<T, __half>::value)
+      c += (__half2float(x) != 0.0f) ? 1 : 0;
+    else
+      c += (x != T(0)) ? 1 : 0;
+  }
   __device__ __forceinline__ void merge(const CountAcc &o) { c += o.c; }
   __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const { store_i(os.out, os.dt, oi, c); }
 };
@@ -217,7 +238,14 @@ struct ExtAcc {
     else
       m = MAX ? (v > m ? v : m) : (v < m ? v : m);
   }
-  __device__ __forceinline__ void merge(const ExtAcc &o) { add((T)o.m, 0); }
+  // merged in the lane type: an empty partial holds the lane type's extreme,
+  // which a narrow T (int8, bool) could not represent
+  __device__ __forceinline__ void merge(const ExtAcc &o) {
+    if constexpr (std::is_floating_point<T>::value)
+      m = MAX ? (Lane<T>)fmax(m, o.m) : (Lane<T>)fmin(m, o.m);
+    else
+      m = MAX ? (o.m > m ? o.m : m) : (o.m < m ? o.m : m);
+  }
   __device__ __forceinline__ void store(const OutSpec &os, int64_t oi) const {
     if constexpr (std::is_floating_point<T>::value)
       store_f(os.out, os.dt, oi, (double)m);

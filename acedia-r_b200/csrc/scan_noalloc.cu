@@ -14,18 +14,27 @@
 // Its scratch is one file-scope __device__ array of kNoAllocScratchBytes
 // (8 MiB), which every GPU that loads the library holds until the process
 // exits.  It has room for the tile flags, the per-tile aggregates and
-// inclusive prefixes, and the ticket counters of the chained-scan kernel:
-// about 1.7 billion elements for a scan along a contiguous axis (20 bytes per
-// 4096-element tile), about 130 million when float32 lanes are interleaved
-// (516 bytes per tile of 32 lanes x 256 steps; a cumsum along the last axis
-// of a 64 x 1048576 float32 matrix needs 4.2 MB).  Larger problems are
+// inclusive prefixes, and the ticket counters of the chained-scan kernel.
+// Along a contiguous axis a tile is 4096 steps and costs 20 bytes: about 1.7
+// billion elements.  With interleaved lanes a tile is 32 float32 lanes x 256
+// steps (516 bytes) or 16 float64 lanes x 512 steps (260 bytes), whatever
+// number of its lanes is real: about 130 million elements when the lane count
+// is a multiple of the tile width, proportionally fewer for narrow lane counts
+// (about 8 million float32 elements with 2 lanes).  A cumsum along the last
+// axis of a 64 x 1048576 float32 matrix needs 4.2 MB.  Larger problems are
 // rejected with ACD_ERR_UNSUPPORTED before anything is launched.
 //
 // Behaviour to know:
 //   * the array's host-side name is not a device address: on the first call on
 //     each device (with that device current) the entry point looks up the
-//     address with cudaGetSymbolAddress and caches it; make that first call
-//     before any stream capture;
+//     address with cudaGetSymbolAddress and caches it for the life of the
+//     process; make that first call before any stream capture, and do not
+//     use the entry point after a cudaDeviceReset of that device (the cached
+//     address would be stale);
+//   * results have acd_scan's semantics; with interleaved lanes acd_scan runs
+//     its reduce-then-scan kernels while this entry point runs the chained
+//     scan, so the additions happen in another order and the results agree
+//     within rounding, not bit for bit;
 //   * every call shares the array and it keeps the last call's contents: each
 //     call clears the counters and flags it relies on (cudaMemsetAsync on the
 //     caller's stream) before launching;

@@ -12,7 +12,9 @@
 
 namespace acd {
 
-static acd_ctx *shim_ctx() {
+// The per-device context of the reference-named launchers (created on first
+// use; also used by the contraction launchers in linalg.cu).
+acd_ctx *shim_ctx() {
   static std::mutex mu;
   static acd_ctx *ctxs[64] = {nullptr};
   int dev = 0;
@@ -86,6 +88,11 @@ template <> constexpr int32_t dt_of<float>() { return ACD_FLOAT32; }
 template <> constexpr int32_t dt_of<double>() { return ACD_FLOAT64; }
 template <> constexpr int32_t dt_of<int32_t>() { return ACD_INT32; }
 template <> constexpr int32_t dt_of<int64_t>() { return ACD_INT64; }
+template <> constexpr int32_t dt_of<__half>() { return ACD_FLOAT16; }
+template <> constexpr int32_t dt_of<int8_t>() { return ACD_INT8; }
+
+static __half *hp(acd_half *p) { return reinterpret_cast<__half *>(p); }
+static const __half *hp(const acd_half *p) { return reinterpret_cast<const __half *>(p); }
 
 template <typename T>
 static void bin(int op, T *r, const T *a, const T *b, size_t n, const char *fn) {
@@ -367,6 +374,65 @@ void tensor_strided_copy_float64(double *dest, const double *src, const int *str
   const acd_desc o = contiguous_of(dest, ACD_FLOAT64, shape, ndims);
   const acd_desc x = from_meta(src, ACD_FLOAT64, strides, shape, ndims);
   shim_done(acd_copy(shim_ctx(), &o, &x, nullptr), "tensor_strided_copy_float64");
+}
+
+// ---- float16 and int8: src/kernels/tensor_ops.cu:1053-1117, 1368-1392 ----
+#define ACD_BIN16(NAME, OP)                                                                     \
+  void tensor_##NAME##_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t n) {   \
+    bin<__half>(OP, hp(r), hp(a), hp(b), n, "tensor_" #NAME "_float16");                        \
+  }                                                                                             \
+  void tensor_##NAME##_strided_float16(const acd_ref_descriptor *o, const acd_ref_descriptor *a, \
+                                       const acd_ref_descriptor *b) {                           \
+    strided_bin<__half>(OP, o, a, b, "tensor_" #NAME "_strided_float16");                       \
+  }
+ACD_BIN16(add, ACD_ADD)
+ACD_BIN16(sub, ACD_SUB)
+ACD_BIN16(mul, ACD_MUL)
+ACD_BIN16(div, ACD_DIV)
+#undef ACD_BIN16
+
+// the scalar arrives as float and rounds once to half, as the reference's
+// convert_type<half>(float) does (src/kernels/tensor_kernels.cu:33-39)
+void tensor_scalar_add_float16(acd_half *r, const acd_half *x, float s, size_t n) {
+  sca<__half>(ACD_ADD, hp(r), hp(x), (double)s, n, "tensor_scalar_add_float16");
+}
+void tensor_scalar_mul_float16(acd_half *r, const acd_half *x, float s, size_t n) {
+  sca<__half>(ACD_MUL, hp(r), hp(x), (double)s, n, "tensor_scalar_mul_float16");
+}
+void tensor_add_int8(int8_t *r, const int8_t *a, const int8_t *b, size_t n) {
+  bin<int8_t>(ACD_ADD, r, a, b, n, "tensor_add_int8");
+}
+void tensor_add_strided_int8(const acd_ref_descriptor *o, const acd_ref_descriptor *a, const acd_ref_descriptor *b) {
+  strided_bin<int8_t>(ACD_ADD, o, a, b, "tensor_add_strided_int8");
+}
+
+// The reference's float16 and int64 sums are placeholders that return 0
+// (src/kernels/tensor_ops.cu:701-710); these compute the sums.
+float tensor_sum_float16(const acd_half *in, size_t n) {
+  if (n == 0) return 0.0f;
+  acd_ctx *c = shim_ctx();
+  double *d = &c->control->stats[4];
+  const acd_desc x = flat(hp(in), ACD_FLOAT16, n);
+  const acd_desc o = flat(d, ACD_FLOAT64, 1);
+  acd_status st = acd_reduce(c, ACD_RED_SUM, &o, &x, 1u, nullptr);
+  double h = 0.0;
+  if (st != ACD_OK) throw std::runtime_error(std::string("tensor_sum_float16: ") + acd_last_error());
+  const cudaError_t e = cudaMemcpy(&h, d, sizeof(double), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("tensor_sum_float16: ") + cudaGetErrorString(e));
+  return (float)h;
+}
+int64_t tensor_sum_int64(const int64_t *in, size_t n) {
+  if (n == 0) return 0;
+  acd_ctx *c = shim_ctx();
+  int64_t *d = reinterpret_cast<int64_t *>(&c->control->stats[5]);
+  const acd_desc x = flat(in, ACD_INT64, n);
+  const acd_desc o = flat(d, ACD_INT64, 1);
+  acd_status st = acd_reduce(c, ACD_RED_SUM, &o, &x, 1u, nullptr);
+  int64_t h = 0;
+  if (st != ACD_OK) throw std::runtime_error(std::string("tensor_sum_int64: ") + acd_last_error());
+  const cudaError_t e = cudaMemcpy(&h, d, sizeof(int64_t), cudaMemcpyDeviceToHost);
+  if (e != cudaSuccess) throw std::runtime_error(std::string("tensor_sum_int64: ") + cudaGetErrorString(e));
+  return h;  // exact modulo 2^64, as the int64 accumulator wraps
 }
 
 float tensor_sum_float32(const float *in, size_t n) { return full_reduce<float>(ACD_RED_SUM, in, n, "tensor_sum_float32"); }

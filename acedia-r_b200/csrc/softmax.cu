@@ -415,6 +415,343 @@ static acd_status launch_softmax_wide(acd_ctx *ctx, SoftArgs a, cudaStream_t s) 
   return ACD_OK;
 }
 
+// ---- one HBM read through L2: statistics and apply as ordered tickets --------
+// For the same views as the wide kernels (contiguous lanes, 16-byte aligned).
+// The lanes are cut into groups of one warp width (GW = 32 * VL lanes, a
+// 512-byte row per step) and the steps into chunks.  Work items are:
+//   A(g, c): the online (max, sum) of group g over chunk c, written as a
+//            per-lane partial; the CTA that completes group g's last chunk
+//            merges the partials into (M, 1/S) per lane and flags the group;
+//   B(g, c): exp(x - M) * (1/S) over chunk c of group g.
+// One persistent launch takes items by a global ticket counter in the order
+//   A(0,*) ; A(1,*) ; ... A(lag,*) B(0,*) ; A(lag+1,*) B(1,*) ; ...
+// so the A items of a group run `lag` groups before its B items, and the
+// input those B items re-read was read by the A items a moment earlier: it
+// is still in L2 (A reads mark it evict_last, B reads and the output stores
+// evict_first), so HBM sees the input once and the output once.  lag is
+// chosen so that the groups between an A and its B, plus the items in
+// flight, stay well inside L2.  A B item waits (bounded, 1 s by
+// %globaltimer, status code 4 when it expires) until its group is flagged;
+// every A item it waits for was taken earlier by a running CTA and never
+// waits itself, so the wait always ends.  Counters are zero at rest: the last
+// B item of a group clears the group's counters and the last CTA to leave
+// clears the ticket counter.
+struct SoftL2Args {
+  const void *in;
+  void *out;
+  int64_t L, R, O;
+  int64_t sr, so, orr, oo;  // lanes are contiguous (stride 1) on both sides
+  int64_t lgroups;          // lane groups per outer index
+  int64_t ng;               // lgroups * O
+  int64_t nchunks, chunk;   // chunks per group, steps per chunk (a multiple of 8)
+  int64_t lag;              // groups between A(g) and B(g)
+  int64_t total;            // tickets: (ng + lag) * 2 * nchunks
+  unsigned int *cnt;        // [3 * ng + 2]: A done, ready, B done per group; ticket; CTAs done
+  void *part;               // [ng][nchunks][GW] (m, s) pairs in T
+  void *stat;               // [ng][GW] (M, 1/S) pairs in T
+  Control *control;
+};
+
+__device__ __forceinline__ uint64_t policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ uint64_t policy_evict_first() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+
+template <typename T>
+__device__ __forceinline__ Vec<T, 16 / sizeof(T)> ld_hint(const T *p, uint64_t pol) {
+  Vec<T, 16 / sizeof(T)> v;
+  if constexpr (sizeof(T) == 4)
+    asm volatile("ld.global.L2::cache_hint.v4.f32 {%0, %1, %2, %3}, [%4], %5;"
+                 : "=f"(v.v[0]), "=f"(v.v[1]), "=f"(v.v[2]), "=f"(v.v[3])
+                 : "l"(p), "l"(pol));
+  else
+    asm volatile("ld.global.L2::cache_hint.v2.f64 {%0, %1}, [%2], %3;"
+                 : "=d"(v.v[0]), "=d"(v.v[1])
+                 : "l"(p), "l"(pol));
+  return v;
+}
+
+template <typename T>
+__device__ __forceinline__ void st_hint(T *p, const Vec<T, 16 / sizeof(T)> &v, uint64_t pol) {
+  if constexpr (sizeof(T) == 4)
+    asm volatile("st.global.L2::cache_hint.v4.f32 [%0], {%1, %2, %3, %4}, %5;" ::"l"(p), "f"(v.v[0]), "f"(v.v[1]),
+                 "f"(v.v[2]), "f"(v.v[3]), "l"(pol)
+                 : "memory");
+  else
+    asm volatile("st.global.L2::cache_hint.v2.f64 [%0], {%1, %2}, %3;" ::"l"(p), "d"(v.v[0]), "d"(v.v[1]), "l"(pol)
+                 : "memory");
+}
+
+__device__ __forceinline__ unsigned int ld_acquire_u32(const unsigned int *p) {
+  unsigned int v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_u32(unsigned int *p, unsigned int v) {
+  asm volatile("st.release.gpu.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+
+// A pair of T read at L2 (never a stale L1 line: the pairs are written by
+// other CTAs of the same launch).
+template <typename T>
+__device__ __forceinline__ Vec<T, 2> ld_pair_cg(const Vec<T, 2> *p) {
+  Vec<T, 2> r;
+  if constexpr (sizeof(T) == 4) {
+    const float2 v = __ldcg(reinterpret_cast<const float2 *>(p));
+    r.v[0] = v.x;
+    r.v[1] = v.y;
+  } else {
+    const double2 v = __ldcg(reinterpret_cast<const double2 *>(p));
+    r.v[0] = v.x;
+    r.v[1] = v.y;
+  }
+  return r;
+}
+
+// (m, s) of one lane: m the maximum, s = sum exp(x - m); merged in double.
+__device__ __forceinline__ void merge_ms(double &M, double &S, double m, double s) {
+  if (m == -INFINITY) return;
+  if (m > M) {
+    S = S * exp(M - m) + s;
+    M = m;
+  } else {
+    S += s * exp(m - M);
+  }
+}
+
+template <typename T, int U>
+__global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
+  constexpr int VL = 16 / sizeof(T);
+  constexpr int GW = 32 * VL;
+  using P = Vec<T, 2>;  // (m, s) or (M, 1/S)
+  __shared__ double red_m[8][GW], red_s[8][GW];
+  __shared__ int64_t s_ticket;
+  __shared__ int s_last;
+  const int warp = threadIdx.x / 32, lane32 = threadIdx.x % 32;
+  const int64_t per_block = 2 * a.nchunks;
+  const int64_t wsteps = a.chunk / 8;  // steps per warp in an item
+  const uint64_t keep = policy_evict_last(), drop = policy_evict_first();
+  P *part = static_cast<P *>(a.part);
+  P *stat = static_cast<P *>(a.stat);
+  unsigned int *cntA = a.cnt, *ready = a.cnt + a.ng, *cntB = a.cnt + 2 * a.ng;
+  unsigned int *ticket = a.cnt + 3 * a.ng, *done = ticket + 1;
+
+  if (threadIdx.x == 0) s_ticket = (int64_t)atomicAdd(ticket, 1u);
+  __syncthreads();
+  int64_t t = s_ticket;
+  while (t < a.total) {
+    const int64_t blk = t / per_block, slot = t % per_block;
+    const bool is_a = slot < a.nchunks;
+    const int64_t g = is_a ? blk : blk - a.lag;
+    const int64_t c = is_a ? slot : slot - a.nchunks;
+    __syncthreads();  // s_ticket, s_last and red_* reuse
+    if (g >= 0 && g < a.ng) {
+      const int64_t o = g / a.lgroups, lg = g % a.lgroups;
+      const int64_t l0 = lg * GW + (int64_t)lane32 * VL;  // first lane of this thread
+      const bool lane_ok = l0 < a.L;                     // L is a multiple of VL
+      int64_t r0 = c * a.chunk + (int64_t)warp * wsteps;
+      int64_t r1 = r0 + wsteps;
+      if (r1 > a.R) r1 = a.R;
+      const T *in = static_cast<const T *>(a.in) + o * a.so + l0;
+      if (is_a) {
+        // ---- A: online (max, sum) in the tensor dtype, U steps per batch
+        T m[VL], sm[VL];
+#pragma unroll
+        for (int k = 0; k < VL; ++k) {
+          m[k] = lowest_of<T>();
+          sm[k] = T(0);
+        }
+        if (lane_ok) {
+          int64_t r = r0;
+          for (; r + U - 1 < r1; r += U) {
+            Vec<T, VL> x[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) x[u] = ld_hint(in + (r + u) * a.sr, keep);
+#pragma unroll
+            for (int k = 0; k < VL; ++k) {
+              T mb = x[0].v[k];
+#pragma unroll
+              for (int u = 1; u < U; ++u) mb = m_max(mb, x[u].v[k]);
+              const T mn = m_max(m[k], mb);
+              if (mn == lowest_of<T>()) continue;  // all -inf so far
+              T acc = (m[k] == lowest_of<T>()) ? T(0) : sm[k] * m_exp(m[k] - mn);
+#pragma unroll
+              for (int u = 0; u < U; ++u) acc += m_exp(x[u].v[k] - mn);
+              sm[k] = acc;
+              m[k] = mn;
+            }
+          }
+          for (; r < r1; ++r) {
+            const Vec<T, VL> x = ld_hint(in + r * a.sr, keep);
+#pragma unroll
+            for (int k = 0; k < VL; ++k) {
+              const T mn = m_max(m[k], x.v[k]);
+              if (mn == lowest_of<T>()) continue;
+              const T acc = (m[k] == lowest_of<T>()) ? T(0) : sm[k] * m_exp(m[k] - mn);
+              sm[k] = acc + m_exp(x.v[k] - mn);
+              m[k] = mn;
+            }
+          }
+        }
+#pragma unroll
+        for (int k = 0; k < VL; ++k) {
+          red_m[warp][lane32 * VL + k] = m[k] == lowest_of<T>() ? -INFINITY : (double)m[k];
+          red_s[warp][lane32 * VL + k] = (double)sm[k];
+        }
+        __syncthreads();
+        // the eight warps' pairs of a lane -> the item's partial (in T)
+        P *dst = part + (g * a.nchunks + c) * GW;
+        for (int i = threadIdx.x; i < GW; i += blockDim.x) {
+          double M = -INFINITY, S = 0.0;
+          for (int w = 0; w < 8; ++w) merge_ms(M, S, red_m[w][i], red_s[w][i]);
+          P pr;
+          pr.v[0] = M == -INFINITY ? lowest_of<T>() : (T)M;
+          pr.v[1] = (T)S;
+          dst[i] = pr;
+        }
+        __threadfence();
+        __syncthreads();
+        if (threadIdx.x == 0) s_last = (atomicAdd(&cntA[g], 1u) == (unsigned int)(a.nchunks - 1));
+        __syncthreads();
+        if (s_last) {
+          // ---- the group's last A item: merge all chunk partials per lane
+          __threadfence();
+          for (int i = threadIdx.x; i < GW; i += blockDim.x) {
+            const P *src = part + g * a.nchunks * GW + i;
+            double M = -INFINITY;
+            for (int64_t q = 0; q < a.nchunks; ++q) {
+              const P v = ld_pair_cg(src + q * GW);
+              if (v.v[0] != lowest_of<T>()) M = fmax(M, (double)v.v[0]);
+            }
+            double S = 0.0;
+            if (M != -INFINITY)
+              for (int64_t q = 0; q < a.nchunks; ++q) {
+                const P v = ld_pair_cg(src + q * GW);
+                if (v.v[0] != lowest_of<T>()) S += (double)v.v[1] * exp((double)v.v[0] - M);
+              }
+            P st;
+            st.v[0] = M == -INFINITY ? lowest_of<T>() : (T)M;
+            st.v[1] = (T)(1.0 / S);
+            stat[g * GW + i] = st;
+          }
+          __threadfence();
+          __syncthreads();
+          if (threadIdx.x == 0) st_release_u32(&ready[g], 1u);
+        }
+      } else {
+        // ---- B: wait for the group's statistics, then write
+        if (threadIdx.x == 0) {
+          if (ld_acquire_u32(&ready[g]) == 0u) {
+            const uint64_t t0 = global_timer_ns();
+            while (ld_acquire_u32(&ready[g]) == 0u) {
+              if (global_timer_ns() - t0 > 1000000000ull) {
+                raise_status(a.control, 4, (int32_t)(g & 0x7fffffff));
+                break;
+              }
+              __nanosleep(200);
+            }
+          }
+        }
+        __syncthreads();
+        T M[VL], inv[VL];
+#pragma unroll
+        for (int k = 0; k < VL; ++k) {
+          const P st = lane_ok ? ld_pair_cg(stat + g * GW + lane32 * VL + k) : P{};
+          M[k] = st.v[0];
+          inv[k] = st.v[1];
+        }
+        T *out = static_cast<T *>(a.out) + o * a.oo + l0;
+        if (lane_ok) {
+          int64_t r = r0;
+          for (; r + U - 1 < r1; r += U) {
+            Vec<T, VL> x[U];
+#pragma unroll
+            for (int u = 0; u < U; ++u) x[u] = ld_hint(in + (r + u) * a.sr, drop);
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              Vec<T, VL> y;
+#pragma unroll
+              for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x[u].v[k] - M[k]) * inv[k];
+              st_hint(out + (r + u) * a.orr, y, drop);
+            }
+          }
+          for (; r < r1; ++r) {
+            const Vec<T, VL> x = ld_hint(in + r * a.sr, drop);
+            Vec<T, VL> y;
+#pragma unroll
+            for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x.v[k] - M[k]) * inv[k];
+            st_hint(out + r * a.orr, y, drop);
+          }
+        }
+        __syncthreads();
+        if (threadIdx.x == 0 && atomicAdd(&cntB[g], 1u) == (unsigned int)(a.nchunks - 1)) {
+          // every B item of the group has read its statistics: clear the counters
+          cntA[g] = 0u;
+          ready[g] = 0u;
+          cntB[g] = 0u;
+        }
+      }
+    }
+    if (threadIdx.x == 0) s_ticket = (int64_t)atomicAdd(ticket, 1u);
+    __syncthreads();
+    t = s_ticket;
+  }
+  if (threadIdx.x == 0 && atomicAdd(done, 1u) == gridDim.x - 1) {
+    *ticket = 0u;  // every CTA has taken its last ticket
+    *done = 0u;
+  }
+}
+
+// Tuning of k_softmax_l2: steps per chunk, CTAs per SM and the lag in
+// groups.  Items of 128 KB; the lag puts about 24 MB of input between a
+// group's A and B items.
+template <typename T>
+static acd_status launch_softmax_l2(acd_ctx *ctx, SoftArgs sa, cudaStream_t s) {
+  constexpr int VL = 16 / sizeof(T);
+  constexpr int64_t GW = 32 * VL;
+  constexpr int64_t row_bytes = GW * sizeof(T);  // 512
+  SoftL2Args a{};
+  a.in = sa.in;
+  a.out = sa.out;
+  a.L = sa.L;
+  a.R = sa.R;
+  a.O = sa.O;
+  a.sr = sa.sr;
+  a.so = sa.so;
+  a.orr = sa.orr;
+  a.oo = sa.oo;
+  a.lgroups = (sa.L + GW - 1) / GW;
+  a.ng = a.lgroups * sa.O;
+  int64_t chunk = (128 * 1024) / row_bytes;  // 256 steps
+  if (chunk > sa.R) chunk = (sa.R + 7) / 8 * 8;
+  a.chunk = chunk;
+  a.nchunks = (sa.R + chunk - 1) / chunk;
+  const int64_t group_bytes = a.nchunks * chunk * row_bytes;
+  a.lag = (24ll << 20) / group_bytes;
+  if (a.lag < 1) a.lag = 1;
+  if (a.lag > a.ng) a.lag = a.ng;
+  a.total = (a.ng + a.lag) * 2 * a.nchunks;
+  if (a.total >= (1ll << 31) || a.ng >= (1ll << 29)) return fail(ACD_ERR_UNSUPPORTED, "softmax: too many items");
+  ACD_TRY(get_counters(ctx, (size_t)(3 * a.ng + 2), s, &a.cnt));
+  const size_t pbytes = sizeof(T) * 2 * (size_t)(a.ng * a.nchunks * GW);
+  const size_t sbytes = sizeof(T) * 2 * (size_t)(a.ng * GW);
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, pbytes + sbytes, s, &scratch));
+  a.part = scratch;
+  a.stat = static_cast<char *>(scratch) + pbytes;
+  a.control = ctx->control;
+  constexpr int U = 8;
+  const int grid = persistent_grid(ctx, k_softmax_l2<T, U>, 256, 0, a.total);
+  k_softmax_l2<T, U><<<grid, 256, 0, s>>>(a);
+  return ACD_OK;
+}
+
 // ---- one read through TMA: a cluster holds a lane block's whole row ---------
 // For lanes contiguous in memory (the row softmax of a column-major matrix)
 // whose R steps x 128 bytes fit the shared memory of a cluster of up to 16
@@ -846,7 +1183,7 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
   // vectors of lanes (measured faster than the cluster kernel on
   // 65536x4096 float32: 0.60 vs 0.77 ms), else the single-read cluster kernel
   if (wide)
-    st = f32 ? launch_softmax_wide<float>(ctx, a, s) : launch_softmax_wide<double>(ctx, a, s);
+    st = f32 ? launch_softmax_l2<float>(ctx, a, s) : launch_softmax_l2<double>(ctx, a, s);
   else if (f32 ? launch_softmax_tma<float>(ctx, a, s) : launch_softmax_tma<double>(ctx, a, s))
     st = ACD_OK;
   else if (a.L == 1)

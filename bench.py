@@ -4,10 +4,13 @@ Default workload (the configuration quoted at 1/2/4/8 GPUs): a float32
 256 x 512 x 32768 tensor (2^32 elements, 16 GiB, N(0,1)), sharded along its
 outermost axis, one step =
     y <- contiguous(permute_view(x, c(3,1,2)))      # transpose kernel
-    z <- y*0.5 + exp(-y^2)                          # fused chain, 5 roundings
-    sum(z), var(z)                                  # shard partials + all-gather
-    argmax(z, axis = 1)                             # keys + MAX all-reduce
-The metric is Gelem/s of the whole job (2^32 / step time, max over ranks).
+    z <- y*0.5 + exp(-y^2)                          # one-pass chain kernel, 5 roundings,
+    sum(z), var(z)                                  #   with the shard's statistics row
+    argmax(z, axis = 1)                             #   and argmax keys
+then one int64 MAX all-reduce of keys and rows (N > 1) and the finish kernel
+(rows merged in rank order, keys decoded).  The metric is Gelem/s of the
+whole job (2^32 / step time, max over ranks).  The one-GPU line also carries
+the per-op reports of the other four configurations (per_config).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl reference]
 
@@ -46,6 +49,8 @@ def parse():
     ap.add_argument("--e2e-steps", type=int, default=4)
     ap.add_argument("--n2", type=int, default=N2, help="extent of the sharded axis (default 32768)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-per-config", action="store_true",
+                    help="skip the per-op reports of the other configurations on the default one-GPU run")
     ap.add_argument("--workload", default="views", choices=["views", "c1", "c2", "c3", "c4"],
                     help="views (default, the sharded strided-views step) or a per-op report of one of the "
                          "other configurations on one GPU")
@@ -250,7 +255,9 @@ def _op(name, fn, nbytes, peak, reps=10, note=None, graph=False):
     return d
 
 
-def run_config_report(a):
+def config_ops(workload, peak):
+    """(workload description, op records) of one configuration's per-op report
+    on the current GPU (c1, c2, c3 or c4)."""
     import numpy as np
     import torch
 
@@ -258,14 +265,10 @@ def run_config_report(a):
     import acediar._lib as L
     import acediar.tensor as Tm
 
-    global _ONLY
-    _ONLY = a.only
-    torch.cuda.set_device(0)
-    peak, peak_kind = peaks()
     g = torch.Generator(device="cuda")
     g.manual_seed(SEED)
     ops = []
-    if a.workload == "c1":
+    if workload == "c1":
         n = 1 << 20
         ta = acd.from_torch(torch.rand(n, generator=g, device="cuda", dtype=torch.float64), (n,), "double")
         tb = acd.from_torch(torch.randn(n, generator=g, device="cuda", dtype=torch.float64), (n,), "double")
@@ -306,7 +309,7 @@ def run_config_report(a):
                        note="launch overhead removed; arrays stay in L2"))
         workload = "elementwise chain + reductions, float64 n=2^20"
         unit_elems = n
-    elif a.workload == "c2":
+    elif workload == "c2":
         R = C = 8192
         X = acd.from_torch(torch.randn(R * C, generator=g, device="cuda"), (R, C), "float")
         r = acd.from_torch(torch.rand(C, generator=g, device="cuda") * 2 - 1, (1, C), "float")
@@ -322,7 +325,7 @@ def run_config_report(a):
         ops.append(_op("count(M) per column", lambda: acd.tensor_count(M, axis=[1]), R * C, peak, graph=True))
         workload = "broadcast + compare, float32 8192x8192 + 1x8192"
         unit_elems = R * C
-    elif a.workload == "c3":
+    elif workload == "c3":
         shp = (4096, 4096, 16)
         n = 4096 * 4096 * 16
         T = acd.from_torch(torch.randn(n, generator=g, device="cuda"), shp, "float")
@@ -373,10 +376,36 @@ def run_config_report(a):
             ops.append({"op": "row sums of f32 softmax", "max_abs_dev_from_1": float(np.abs(rows - 1).max())})
         workload = "row softmax float32 65536x4096 (N(0,4) + row offset U(-50,50)), float64 1024x32768"
         unit_elems = R * C
-    ops = [o for o in ops if o is not None]
+    del unit_elems
+    return workload, [o for o in ops if o is not None]
+
+
+def run_config_report(a):
+    import torch
+
+    global _ONLY
+    _ONLY = a.only
+    torch.cuda.set_device(0)
+    peak, peak_kind = peaks()
+    workload, ops = config_ops(a.workload, peak)
     line = {"metric": "HBM GB/s per op (algorithmic bytes / CUDA-event time)", "workload": workload,
             "peak_GB/s": peak, "peak_source": peak_kind, "ops": ops, "n_gpus": 1}
     print(json.dumps(line), flush=True)
+
+
+def per_config_block(peak):
+    """The per-op reports of the four other configurations, compact, for the
+    default one-GPU line: op -> [device ms, fraction of the HBM peak]."""
+    import torch
+    out = {}
+    for w in ("c1", "c2", "c3", "c4"):
+        workload, ops = config_ops(w, peak)
+        out[w] = {"workload": workload,
+                  "ops": {o["op"]: ([o["ms"], o["frac"]] if "ms" in o else {k: v for k, v in o.items() if k != "op"})
+                          for o in ops}}
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+    return out
 
 
 # ---------------------------------------------------------------------------
@@ -425,9 +454,14 @@ def main():
     xp_view = acediar.permute_view(x, [3, 1, 2])
     y = _alloc((n2l, N0, N1), "float", dev)
     z = _alloc((n2l, N0, N1), "float", dev)
-    stats = torch.empty(SH.STATS_WIDTH, dtype=torch.float64, device=dev)
-    gathered = torch.empty((world, SH.STATS_WIDTH), dtype=torch.float64, device=dev)
-    keys = torch.empty(N0 * N1, dtype=torch.int64, device=dev)
+    # one int64 exchange buffer: the argmax keys, then one statistics row per
+    # rank; a single MAX all-reduce carries both (acediar.sharded)
+    nkeys = N0 * N1
+    xbuf = SH.exchange_buffer(nkeys, world, dev)
+    row_ptr = SH.row_slot(xbuf, nkeys, rank)
+    keys_ptr = ctypes.c_void_p(xbuf.data_ptr())
+    sum_var = torch.empty(2, dtype=torch.float64, device=dev)
+    sv_ptr = ctypes.c_void_p(sum_var.data_ptr())
     idx = _alloc((N0, N1), "int32", dev)
     d_xp, d_y, d_z, d_idx = xp_view.desc(), y.desc(), z.desc(), idx.desc()
     pref = ctypes.byref
@@ -440,10 +474,18 @@ def main():
 
     def k_chain_stats_keys(s):
         # z = y*0.5 + exp(-y^2), with this shard's statistics row of z and the
-        # argmax keys of z along axis 1 from the same pass (z is not re-read)
-        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5),
-                                         ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(keys.data_ptr()), lo, s),
+        # argmax keys of z along axis 1 from the same pass (z is not re-read),
+        # written straight into the exchange buffer
+        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5), row_ptr, keys_ptr, lo, s),
                 "fused_stats_keys")
+
+    def exchange():
+        if world > 1:
+            dist.all_reduce(xbuf, op=dist.ReduceOp.MAX)
+
+    def k_finish(s):
+        # argmax indices, and the rows merged in rank order into (sum, var)
+        L.check(lib.acd_shard_finish(ctx, keys_ptr, nkeys, world, pref(d_idx), sv_ptr, 1, s), "shard_finish")
 
     def step(dx=None, input_read=None):
         s = stream()
@@ -451,17 +493,10 @@ def main():
         if input_read is not None:
             input_read.record()  # the transpose is the only reader of the input
         k_chain_stats_keys(s)
-        if world > 1:
-            dist.all_gather_into_tensor(gathered, stats)
-            dist.all_reduce(keys, op=dist.ReduceOp.MAX)
-            rows = gathered
-        else:
-            rows = stats.view(1, -1)
-        tot, var = SH.merge_stats_torch(rows)
-        L.check(lib.acd_argmax_keys_decode(ctx, pref(d_idx), ctypes.c_void_p(keys.data_ptr()), 1, s), "decode")
-        return tot, var
+        exchange()
+        k_finish(stream())
 
-    LAUNCHES_PER_STEP = 3  # transpose, chain with statistics and keys, key decode
+    LAUNCHES_PER_STEP = 3  # transpose, chain with statistics and keys, exchange finish
 
     def barrier():
         torch.cuda.synchronize()
@@ -479,7 +514,7 @@ def main():
     barrier()
     e0.record()
     for _ in range(a.steps):
-        tot, var = step()
+        step()
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1) / a.steps
@@ -488,8 +523,31 @@ def main():
     if world > 1:
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
     ms_max = float(t.item())
-    result_sum, result_var = float(tot.item()), float(var.item())
+    result_sum, result_var = (float(v) for v in sum_var.cpu().tolist())
     idx_host = idx.storage[:N0 * N1].cpu()
+
+    # ---- phase split of the step (CUDA events on the launching stream; the
+    # synchronous all-reduce makes that stream wait for NCCL's), max over ranks
+    PH = 5
+    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(PH)]
+    barrier()
+    for k in range(PH):
+        pev[k][0].record()
+        k_transpose(stream())
+        pev[k][1].record()
+        k_chain_stats_keys(stream())
+        pev[k][2].record()
+        exchange()
+        pev[k][3].record()
+        k_finish(stream())
+        pev[k][4].record()
+    barrier()
+    names = ["transpose", "chain_stats_keys", "exchange", "finish"]
+    ph = torch.tensor([sum(pev[k][j].elapsed_time(pev[k][j + 1]) for k in range(PH)) / PH for j in range(4)],
+                      dtype=torch.float64, device=dev)
+    if world > 1:
+        dist.all_reduce(ph, op=dist.ReduceOp.MAX)
+    phases = {n: round(float(v), 4) for n, v in zip(names, ph.tolist())}
     result_idx = {"checksum": int(idx_host.to(torch.int64).sum().item()), "first": int(idx_host[0].item()),
                   "last": int(idx_host[-1].item())}
 
@@ -529,7 +587,6 @@ def main():
         bufs = [(x.storage, d_xp), (x2.storage, d_xp2)]
         idx_h = torch.empty(N0 * N1, dtype=torch.int32, pin_memory=True)
         res_h = torch.empty(2, dtype=torch.float64, pin_memory=True)
-        res_d = torch.empty(2, dtype=torch.float64, device=dev)
         cs = torch.cuda.Stream(device=dev)
         copied = [torch.cuda.Event(), torch.cuda.Event()]
         read = [torch.cuda.Event(), torch.cuda.Event()]
@@ -552,10 +609,8 @@ def main():
                 issue_copy(k + 1)
             b = k % 2
             torch.cuda.current_stream().wait_event(copied[b])
-            tot2, var2 = step(bufs[b][1], read[b])
-            res_d[0] = tot2
-            res_d[1] = var2
-            res_h.copy_(res_d, non_blocking=True)
+            step(bufs[b][1], read[b])
+            res_h.copy_(sum_var, non_blocking=True)
             idx_h.copy_(idx.storage[:N0 * N1], non_blocking=True)
         f1.record()
         barrier()
@@ -568,7 +623,7 @@ def main():
                "h2d_bytes_per_step": nloc * 4 * world, "d2h_bytes_per_step": (16 + N0 * N1 * 4) * world,
                "ms_per_step": round(ems, 3), "steps": a.e2e_steps,
                "overlap": "input copy of step k+1 under the kernels of step k (two input buffers)"}
-        del x2
+        del x2, bufs, xh
 
     cpu = None
     if rank == 0 and world == 1 and not a.no_cpu_baseline:
@@ -576,6 +631,14 @@ def main():
             cpu = cpu_baseline_single()
         except Exception as ex:  # the baseline is reported, never required
             cpu = {"value": None, "error": str(ex)[:200]}
+
+    # ---- the other configurations' per-op reports (one GPU)
+    per_config = None
+    if world == 1 and not a.no_per_config:
+        del x, y, z, xbuf, xp_view
+        torch.cuda.synchronize()
+        torch.cuda.empty_cache()
+        per_config = per_config_block(peak)
 
     if rank == 0:
         value = ntot / (ms_max * 1e-3) / 1e9
@@ -588,17 +651,18 @@ def main():
             "config": {"workload": "strided views 256x512x%d f32, sharded on axis 3" % n2,
                        "l2": "inputs larger than L2 (16 GiB), no flush needed",
                        "parallelism": "shard%d" % world, "elements": ntot},
-            "algorithmic_GB/s": round(24 * ntot / (ms_max * 1e-3) / 1e9, 1),
             "roofline": {"bound": "hbm", "achieved": top["GB/s"], "peak": peak, "unit": "GB/s",
                          "frac": round(top["GB/s"] / peak, 4), "traffic": top["traffic"], "kernel": top["kernel"],
                          "peak_source": peak_kind, "traffic_source": "ncu dram bytes/elem of the 256x512x1024 "
                          "case x elements per launch"},
             "ops": ops,
+            "phases_ms": phases,
             "gpu_launches": LAUNCHES_PER_STEP * a.steps,
             "clocks": clk,
             "e2e": e2e,
             "cpu_baseline": cpu,
             "result": {"sum": result_sum, "var": result_var, "argmax_axis1": result_idx},
+            "per_config": per_config,
         }
         print(json.dumps(line), flush=True)
     if world > 1:

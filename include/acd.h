@@ -36,13 +36,25 @@ extern "C" {
 
 #define ACD_MAX_DIMS 8
 
-/* Element types.  Names follow dtype_to_string (src/gpuTensor.h:183-200). */
+/* Element types.  Names follow dtype_to_string (src/gpuTensor.h:183-200).
+ * FLOAT16 and INT8 are the reference's two narrow storage types
+ * (DType::FLOAT16 / DType::INT8, src/gpuTensor.h:61-75).  They take the
+ * element-wise arithmetic, scalar ops, comparisons, copies, conversions,
+ * fills and the sum / mean / count reductions (INT8 also max / min);
+ * the transcendental functions, variance, products and arg-reductions
+ * return ACD_ERR_UNSUPPORTED for them.  FLOAT16 arithmetic is IEEE
+ * binary16 with one rounding per operation (the operation is evaluated in
+ * float32 and rounded once, which equals the correctly rounded half result
+ * for + - * /); INT8 arithmetic wraps modulo 256 as the reference's int8_t
+ * arithmetic does. */
 typedef enum {
   ACD_FLOAT32 = 0, /* "float"  */
   ACD_FLOAT64 = 1, /* "double" */
   ACD_INT32 = 2,   /* "int32"  */
   ACD_INT64 = 3,   /* "int64"  */
-  ACD_BOOL = 4     /* "bool", one byte holding 0 or 1 */
+  ACD_BOOL = 4,    /* "bool", one byte holding 0 or 1 */
+  ACD_FLOAT16 = 5, /* "float16", IEEE binary16 */
+  ACD_INT8 = 6     /* "int8"   */
 } acd_dtype;
 
 typedef enum {
@@ -152,7 +164,8 @@ acd_status acd_ctx_set_allocator(acd_ctx *ctx, acd_alloc_fn alloc, acd_free_fn f
 /* Reads and clears the device status word (synchronises `stream`).
  * Returns ACD_ERR_DEVICE and fills *code when a kernel reported an error:
  * 1 = the scan's look-back wait expired, 2 = a wait of the TMA transpose
- * pipeline expired, 3 = the TMA load wait of the cluster softmax expired. */
+ * pipeline expired, 3 = the TMA load wait of the cluster softmax expired,
+ * 4 = the row softmax's wait for a lane group's statistics expired. */
 acd_status acd_ctx_check(acd_ctx *ctx, acd_stream stream, int32_t *code);
 /* Test hook for the bounded look-back wait of the scan: when `tile` >= 0,
  * the scan kernel's tile with that index never publishes its prefix, so the
@@ -268,7 +281,7 @@ acd_status acd_arg_reduce(acd_ctx *ctx, int32_t op, const acd_desc *out_index,
 /* ---- scans and softmax ------------------------------------------------- */
 /* Cumulative sum/product along `axis`, or over the column-major flattened
  * tensor when axis < 0 (cumsum.gpuTensor, R/gpuTensor.R:2234-2277).
- * Accumulates in float64 (float64 input: compensated float64). */
+ * Accumulates in float64 and rounds each output once to the tensor dtype. */
 acd_status acd_scan(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis,
                     acd_stream stream);
 /* exp(x - max) / sum(exp(x - max)) along `axis`; axis < 0 normalises the
@@ -276,15 +289,20 @@ acd_status acd_scan(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_des
 acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, int32_t axis,
                        acd_stream stream);
 
-/* Cumulative sum/product exactly as acd_scan, for callers that cannot
+/* Cumulative sum/product with acd_scan's semantics, for callers that cannot
  * allocate device memory (no context, no workspace): the scratch is a static
- * 8 MiB device array held by every GPU that loads this library.  Problems
- * whose scratch would not fit (about 1.7e9 elements along a contiguous axis,
- * 1.3e8 with interleaved float32 lanes) return ACD_ERR_UNSUPPORTED.  Runs on
- * the current device; the first call on a device looks up the array's device
- * address, so make it before any stream capture.  Calls that overlap on the
- * GPU race on the shared array.  This entry point has no counterpart in the
- * reference. */
+ * 8 MiB device array held by every GPU that loads this library.  With
+ * interleaved lanes the additions run in another order than acd_scan's, so
+ * the two agree within rounding (tested to 1e-5 / 1e-12 relative).  Problems
+ * whose scratch would not fit return ACD_ERR_UNSUPPORTED: about 1.7e9
+ * elements along a contiguous axis; with interleaved lanes 516 (float32) or
+ * 260 (float64) bytes per tile of 32 x 256 or 16 x 512 lane-steps, however
+ * many of its lanes are real (1.3e8 float32 elements when the lane count is a
+ * multiple of 32, 8e6 with 2 lanes).  Runs on the current device; the first
+ * call on a device looks up the array's device address and keeps it for the
+ * process, so make that call before any stream capture and do not use the
+ * entry point after a cudaDeviceReset.  Calls that overlap on the GPU race on
+ * the shared array.  This entry point has no counterpart in the reference. */
 acd_status acd_scan_noalloc(int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis, acd_stream stream);
 
 /* ---- sharded partials (multi-GPU global sum/var and argmax) ------------- */
@@ -318,6 +336,23 @@ acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_des
 acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const acd_desc *z, const acd_desc *in,
                                         double p0, double *stats, int64_t *keys, int64_t index_base,
                                         acd_stream stream);
+/* One exchange for the sharded step.  buf is an int64 array of nkeys + 6 *
+ * world entries: the argmax keys, then one statistics row per rank (the
+ * float64 row of acd_stats_partial stored as bit patterns).  Each rank
+ * passes keys = buf and stats = (double *)(buf + nkeys + 6 * rank) to
+ * acd_fused_stats_keys; the other ranks' rows hold INT64_MIN (the bit
+ * pattern of -0.0, the smallest int64), so a single int64 MAX all-reduce
+ * over the whole buffer selects every key's winner and copies every rank's
+ * row to all ranks.  acd_shard_exchange_init sets all rows to INT64_MIN
+ * once; acd_shard_finish then decodes the keys into out_index (as
+ * acd_argmax_keys_decode), merges the rows in rank order into
+ * sum_var[0] = sum and sum_var[1] = sample variance (device float64[2]),
+ * and sets the rows back to INT64_MIN for the next exchange.  The
+ * reference computes the global sum, var and argmax of one device's tensor
+ * (src/kernels/tensor_ops.cu:785-880); the exchange has no counterpart. */
+acd_status acd_shard_exchange_init(acd_ctx *ctx, int64_t *buf, int64_t nkeys, int32_t world, acd_stream stream);
+acd_status acd_shard_finish(acd_ctx *ctx, int64_t *buf, int64_t nkeys, int32_t world, const acd_desc *out_index,
+                            double *sum_var, int32_t one_based, acd_stream stream);
 /* Decodes keys back to indices (INT32/INT64 out, 1-based when one_based). */
 acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const int64_t *keys,
                                   int32_t one_based, acd_stream stream);

@@ -46,6 +46,62 @@ typedef struct acd_ref_descriptor {
   size_t total_size;
 } acd_ref_descriptor;
 
+/* IEEE binary16 storage: CUDA's `half` (__half), two bytes.  The reference
+ * declares these launchers with `half *`; a pointer to this struct has the
+ * same representation, and extern "C" names carry no parameter types. */
+typedef struct acd_half {
+  uint16_t bits;
+} acd_half;
+
+/* ---- float16 and int8 (declared at src/TensorArithmetic.cpp:13-31, 64-67,
+ * 84-114; defined at src/kernels/tensor_ops.cu:1053-1117, 1368-1392).
+ * float16: one rounding per operation (correctly rounded binary16); the
+ * scalar is rounded to half first.  int8: wraps modulo 256. ---- */
+void tensor_add_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t n);
+void tensor_sub_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t n);
+void tensor_mul_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t n);
+void tensor_div_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t n);
+void tensor_scalar_add_float16(acd_half *r, const acd_half *x, float s, size_t n);
+void tensor_scalar_mul_float16(acd_half *r, const acd_half *x, float s, size_t n);
+void tensor_add_int8(int8_t *r, const int8_t *a, const int8_t *b, size_t n);
+void tensor_add_strided_float16(const acd_ref_descriptor *out, const acd_ref_descriptor *a,
+                                const acd_ref_descriptor *b);
+void tensor_sub_strided_float16(const acd_ref_descriptor *out, const acd_ref_descriptor *a,
+                                const acd_ref_descriptor *b);
+void tensor_mul_strided_float16(const acd_ref_descriptor *out, const acd_ref_descriptor *a,
+                                const acd_ref_descriptor *b);
+void tensor_div_strided_float16(const acd_ref_descriptor *out, const acd_ref_descriptor *a,
+                                const acd_ref_descriptor *b);
+void tensor_add_strided_int8(const acd_ref_descriptor *out, const acd_ref_descriptor *a,
+                             const acd_ref_descriptor *b);
+/* sums (declared at src/TensorReduction.cpp:12-15; the reference's own
+ * definitions, src/kernels/tensor_ops.cu:701-710, are placeholders returning
+ * 0): float16 accumulated in float64 and returned as float; int64 exact
+ * (modulo 2^64) */
+float tensor_sum_float16(const acd_half *in, size_t n);
+int64_t tensor_sum_int64(const int64_t *in, size_t n);
+
+/* ---- contractions (declared at src/TensorLinearAlgebra.cpp:15-34, defined
+ * at src/kernels/tensor_ops.cu:1180-1326): outside the hot path, exported so
+ * the Rcpp modules link against this library alone.  matmul / matvec /
+ * vecmat call cuBLAS (loaded on first use); the outer product
+ * result[i + M*j] = a[i] * b[j] is a broadcast multiply.  Column-major:
+ * C (M x N) = A (M x K) B (K x N); matvec r = A (M x N) v; vecmat
+ * r = v A (M x N).  float16 accumulates in float32.  The float16 matvec and
+ * vecmat are declared but not defined by the reference. ---- */
+void tensor_matmul_float16(acd_half *C, const acd_half *A, const acd_half *B, size_t M, size_t N, size_t K);
+void tensor_matmul_float32(float *C, const float *A, const float *B, size_t M, size_t N, size_t K);
+void tensor_matmul_float64(double *C, const double *A, const double *B, size_t M, size_t N, size_t K);
+void tensor_outer_product_float16(acd_half *r, const acd_half *a, const acd_half *b, size_t M, size_t N);
+void tensor_outer_product_float32(float *r, const float *a, const float *b, size_t M, size_t N);
+void tensor_outer_product_float64(double *r, const double *a, const double *b, size_t M, size_t N);
+void tensor_matvec_float16(acd_half *r, const acd_half *A, const acd_half *v, size_t M, size_t N);
+void tensor_matvec_float32(float *r, const float *A, const float *v, size_t M, size_t N);
+void tensor_matvec_float64(double *r, const double *A, const double *v, size_t M, size_t N);
+void tensor_vecmat_float16(acd_half *r, const acd_half *v, const acd_half *A, size_t M, size_t N);
+void tensor_vecmat_float32(float *r, const float *v, const float *A, size_t M, size_t N);
+void tensor_vecmat_float64(double *r, const double *v, const double *A, size_t M, size_t N);
+
 /* ---- contiguous elementwise: src/kernels/tensor_ops.cu:1001-1117 ---- */
 void tensor_add_float32(float *r, const float *a, const float *b, size_t n);
 void tensor_add_float64(double *r, const double *a, const double *b, size_t n);

@@ -38,7 +38,9 @@
 
 #define MAXD 8
 
-enum { DT_F32 = 0, DT_F64 = 1, DT_I32 = 2, DT_I64 = 3, DT_BOOL = 4 };
+/* DT_F16 is IEEE binary16 (_Float16: gcc converts to and from it with one
+ * rounding to nearest); DT_I8 is int8_t (no NA; arithmetic wraps modulo 256) */
+enum { DT_F32 = 0, DT_F64 = 1, DT_I32 = 2, DT_I64 = 3, DT_BOOL = 4, DT_F16 = 5, DT_I8 = 6 };
 enum {
   U_EXP = 0, U_LOG, U_SQRT, U_ABS, U_FLOOR, U_CEIL, U_ROUND, U_ERF, U_TANH, U_SIGMOID, U_RELU, U_SIN, U_COS,
   U_NEG, U_SQUARE, U_COPY
@@ -55,6 +57,8 @@ static long double ld_get(const void *p, int dt, int64_t i) {
     case DT_I32: return ((const int32_t *)p)[i];
     case DT_I64: return (long double)((const int64_t *)p)[i];
     case DT_BOOL: return ((const uint8_t *)p)[i];
+    case DT_F16: return ((const _Float16 *)p)[i];
+    case DT_I8: return ((const int8_t *)p)[i];
   }
   return 0.0L;
 }
@@ -64,6 +68,7 @@ static long double rnd(long double v, int dt) {
   switch (dt) {
     case DT_F32: return (float)v;
     case DT_F64: return (double)v;
+    case DT_F16: return (_Float16)v;
     default: return v;
   }
 }
@@ -75,6 +80,8 @@ static void put(void *p, int dt, int64_t i, long double v) {
     case DT_I32: ((int32_t *)p)[i] = (int32_t)v; break;
     case DT_I64: ((int64_t *)p)[i] = (int64_t)v; break;
     case DT_BOOL: ((uint8_t *)p)[i] = (uint8_t)(v != 0.0L); break;
+    case DT_F16: ((_Float16 *)p)[i] = (_Float16)v; break;
+    case DT_I8: ((int8_t *)p)[i] = (int8_t)(int64_t)v; break; /* wraps modulo 256 */
   }
 }
 
@@ -98,26 +105,31 @@ static int64_t offset_of(int64_t idx, int nd, const int64_t *shape, const int64_
  * native IEEE operation (computing in long double and rounding afterwards
  * could round twice) */
 static long double add_dt(long double a, long double b, int dt) {
+  if (dt == DT_F16) return (_Float16)(a + b); /* exact (or 64-bit) in long double, one rounding */
   if (dt == DT_F32) return (float)a + (float)b;
   if (dt == DT_F64) return (double)a + (double)b;
   return a + b;
 }
 static long double sub_dt(long double a, long double b, int dt) {
+  if (dt == DT_F16) return (_Float16)(a - b); /* exact (or 64-bit) in long double, one rounding */
   if (dt == DT_F32) return (float)a - (float)b;
   if (dt == DT_F64) return (double)a - (double)b;
   return a - b;
 }
 static long double mul_dt(long double a, long double b, int dt) {
+  if (dt == DT_F16) return (_Float16)(a * b); /* exact (or 64-bit) in long double, one rounding */
   if (dt == DT_F32) return (float)a * (float)b;
   if (dt == DT_F64) return (double)a * (double)b;
   return a * b;
 }
 static long double div_dt(long double a, long double b, int dt) {
+  if (dt == DT_F16) return (_Float16)(a / b); /* exact (or 64-bit) in long double, one rounding */
   if (dt == DT_F32) return (float)a / (float)b;
   if (dt == DT_F64) return (double)a / (double)b;
   return a / b;
 }
 static long double sqrt_dt(long double x, int dt) {
+  if (dt == DT_F16) return (_Float16)sqrtl(x);
   if (dt == DT_F32) return sqrtf((float)x);
   if (dt == DT_F64) return sqrt((double)x);
   return sqrtl(x);
@@ -245,25 +257,34 @@ void orc_copy(int dt, const void *in, int nd, const int64_t *shape, const int64_
  * src/kernels/tensor_kernels.cu:52-57 and src/kernels/kernel_utils.cuh:11;
  * R's as.integer truncates toward zero and gives NA for NaN and out-of-range
  * values; NA integers are INT32_MIN / INT64_MIN and convert to NaN). */
+static int is_fp(int dt) { return dt == DT_F32 || dt == DT_F64 || dt == DT_F16; }
+
+/* the source value as a long double (exact for every dtype), NA integers as NaN;
+ * int8 has no NA */
+static long double conv_src(int from, const void *in, int64_t off) {
+  if (from == DT_I32) {
+    const int32_t x = ((const int32_t *)in)[off];
+    return x == INT32_MIN ? (long double)NAN : (long double)x;
+  }
+  if (from == DT_I64) {
+    const int64_t x = ((const int64_t *)in)[off];
+    return x == INT64_MIN ? (long double)NAN : (long double)x; /* exact in long double */
+  }
+  return ld_get(in, from, off);
+}
+
 static void convert_one(int from, int to, const void *in, int64_t off, void *out, int64_t i) {
-  if (to == DT_F32 || to == DT_F64) {
-    long double v;
-    if (from == DT_I32) {
-      const int32_t x = ((const int32_t *)in)[off];
-      v = x == INT32_MIN ? (long double)NAN : (long double)x;
-    } else if (from == DT_I64) {
-      const int64_t x = ((const int64_t *)in)[off];
-      v = x == INT64_MIN ? (long double)NAN : (long double)x; /* exact in long double */
-    } else {
-      v = ld_get(in, from, off);
-    }
+  if (to == DT_F32 || to == DT_F64 || to == DT_F16) {
+    const long double v = conv_src(from, in, off); /* one rounding below: v is the exact source value */
     if (to == DT_F32)
-      ((float *)out)[i] = (float)v; /* one rounding: v holds the source value exactly */
-    else
+      ((float *)out)[i] = (float)v;
+    else if (to == DT_F64)
       ((double *)out)[i] = (double)v;
+    else
+      ((_Float16 *)out)[i] = (_Float16)v;
   } else if (to == DT_I32) {
     int32_t r;
-    if (from == DT_F32 || from == DT_F64) {
+    if (is_fp(from)) {
       const long double x = ld_get(in, from, off);
       r = (x > -2147483648.0L && x < 2147483648.0L) ? (int32_t)truncl(x) : INT32_MIN;
     } else if (from == DT_I64) {
@@ -271,13 +292,15 @@ static void convert_one(int from, int to, const void *in, int64_t off, void *out
       r = (x >= -2147483647LL && x <= 2147483647LL) ? (int32_t)x : INT32_MIN;
     } else if (from == DT_BOOL) {
       r = ((const uint8_t *)in)[off];
+    } else if (from == DT_I8) {
+      r = ((const int8_t *)in)[off];
     } else {
       r = ((const int32_t *)in)[off];
     }
     ((int32_t *)out)[i] = r;
   } else if (to == DT_I64) {
     int64_t r;
-    if (from == DT_F32 || from == DT_F64) {
+    if (is_fp(from)) {
       const long double x = ld_get(in, from, off);
       r = (x > -9223372036854775808.0L && x < 9223372036854775808.0L) ? (int64_t)truncl(x) : INT64_MIN;
     } else if (from == DT_I32) {
@@ -285,17 +308,39 @@ static void convert_one(int from, int to, const void *in, int64_t off, void *out
       r = x == INT32_MIN ? INT64_MIN : (int64_t)x;
     } else if (from == DT_BOOL) {
       r = ((const uint8_t *)in)[off];
+    } else if (from == DT_I8) {
+      r = ((const int8_t *)in)[off];
     } else {
       r = ((const int64_t *)in)[off];
     }
     ((int64_t *)out)[i] = r;
+  } else if (to == DT_I8) {
+    /* no NA: from a floating value truncate toward zero and saturate to
+     * [-128, 127], NaN -> 0 (the device's float-to-int8 cast); from a wider
+     * integer keep the low 8 bits */
+    int8_t r;
+    if (is_fp(from)) {
+      const long double x = ld_get(in, from, off);
+      r = isnan(x) ? 0 : (x <= -128.0L ? -128 : (x >= 127.0L ? 127 : (int8_t)truncl(x)));
+    } else if (from == DT_I32) {
+      r = (int8_t)(uint8_t)(((const int32_t *)in)[off] & 0xFF);
+    } else if (from == DT_I64) {
+      r = (int8_t)(uint8_t)(((const int64_t *)in)[off] & 0xFF);
+    } else if (from == DT_BOOL) {
+      r = (int8_t)((const uint8_t *)in)[off];
+    } else {
+      r = ((const int8_t *)in)[off];
+    }
+    ((int8_t *)out)[i] = r;
   } else { /* bool: x != 0, so NaN and NA integers give 1 */
     int nz;
     switch (from) {
       case DT_F32: nz = ((const float *)in)[off] != 0.0f; break;
       case DT_F64: nz = ((const double *)in)[off] != 0.0; break;
+      case DT_F16: nz = ((const _Float16 *)in)[off] != 0; break;
       case DT_I32: nz = ((const int32_t *)in)[off] != 0; break;
       case DT_I64: nz = ((const int64_t *)in)[off] != 0; break;
+      case DT_I8: nz = ((const int8_t *)in)[off] != 0; break;
       default: nz = ((const uint8_t *)in)[off] != 0; break;
     }
     ((uint8_t *)out)[i] = (uint8_t)nz;

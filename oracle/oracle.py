@@ -24,7 +24,7 @@ _LIB = None
 _LIB_MT = None
 
 DT = {np.dtype(np.float32): 0, np.dtype(np.float64): 1, np.dtype(np.int32): 2, np.dtype(np.int64): 3,
-      np.dtype(np.uint8): 4, np.dtype(np.bool_): 4}
+      np.dtype(np.uint8): 4, np.dtype(np.bool_): 4, np.dtype(np.float16): 5, np.dtype(np.int8): 6}
 UNARY = {n: i for i, n in enumerate(
     ["exp", "log", "sqrt", "abs", "floor", "ceil", "round", "erf", "tanh", "sigmoid", "relu", "sin", "cos",
      "neg", "square", "copy"])}

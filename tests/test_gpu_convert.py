@@ -69,5 +69,7 @@ def test_convert_aliases_and_errors(acd):
     assert acd.to_dtype(t, "int").dtype == "int32"
     assert acd.to_dtype(t, "float32").dtype == "float"
     assert acd.to_dtype(t, "long").dtype == "int64"
-    with pytest.raises(ValueError, match="Unsupported target dtype: int8"):
-        acd.to_dtype(t, "int8")
+    assert acd.to_dtype(t, "half").dtype == "float16"
+    assert acd.to_dtype(t, "int8").dtype == "int8"
+    with pytest.raises(ValueError, match="Unsupported target dtype: uint16"):
+        acd.to_dtype(t, "uint16")

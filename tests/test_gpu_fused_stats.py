@@ -107,3 +107,45 @@ def test_fused_stats_keys_infinities_and_nan(acd):
     keys_ref, _ = SH.argmax_keys(z_ref, 0, 3)
     assert torch.equal(keys.cpu(), keys_ref.cpu()), (keys.cpu(), keys_ref.cpu())
     assert np.isnan(stats.cpu().numpy()[2]) and np.isnan(SH.stats_partial(z_ref).cpu().numpy()[2])
+
+
+@pytest.mark.parametrize("world", [1, 3])
+def test_shard_exchange_on_one_gpu(acd, world):
+    """The one-collective exchange with `world` shards emulated on one GPU:
+    each shard's one-pass chain kernel writes its keys and its statistics row
+    into its own exchange buffer, torch.maximum over the buffers stands in for
+    the MAX all-reduce, and acd_shard_finish gives the argmax along the
+    permuted axis (exact, ties across shards included) and the global sum and
+    var (float32 contract) of the whole tensor; the rows are reset after."""
+    import ctypes
+
+    import acediar._lib as L
+    import acediar.sharded as SH
+    from acediar.tensor import _alloc, _stream, context
+
+    rng = np.random.default_rng(40 + world)
+    n0, n1, n2 = 64, 48, 96
+    x = (np.round(rng.normal(0, 1, (n0, n1, n2)) * 4) / 4).astype(np.float32)  # ties, across shards too
+    nkeys = n0 * n1
+    bufs = []
+    for r in range(world):
+        lo, hi = SH.shard_bounds(n2, r, world)
+        xs = acd.as_tensor(np.ascontiguousarray(x[:, :, lo:hi]), dtype="float")
+        y = acd.contiguous(acd.permute_view(xs, [3, 1, 2]))
+        buf = SH.exchange_buffer(nkeys, world, y.storage.device)
+        z = _alloc(y.shape, "float")
+        L.check(L.lib().acd_fused_stats_keys(context(), ctypes.byref(z.desc()), ctypes.byref(y.desc()),
+                                             ctypes.c_double(0.5), SH.row_slot(buf, nkeys, r),
+                                             ctypes.c_void_p(buf.data_ptr()), lo, _stream()), "fused_stats_keys")
+        bufs.append(buf)
+    red = bufs[0].clone()
+    for b in bufs[1:]:
+        red = torch.maximum(red, b)
+    idx, sv = SH.shard_finish(red, nkeys, world, (n0, n1))
+    z_all = oracle.gauss_chain(np.transpose(x, (2, 0, 1)), 0.5)
+    es, ev = oracle.sum_var(z_all)
+    tot, var = (float(v) for v in sv.cpu().numpy())
+    assert abs(tot - es) <= 1e-5 * max(1.0, np.abs(z_all.astype(np.float64)).sum())
+    assert abs(var - ev) <= 1e-5 * abs(ev)
+    assert_exact(idx.as_array().astype(np.int64), oracle.arg_reduce("argmax", z_all, 0), "argmax keys across shards")
+    assert torch.all(red[nkeys:] == np.iinfo(np.int64).min), "rows reset for the next exchange"

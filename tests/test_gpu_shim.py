@@ -119,7 +119,8 @@ def test_mutation_and_assembly_names(lib):
     z[2:4, 3:5] = src
     assert_exact(d64.cpu().numpy(), z.reshape(-1, order="F"), "tensor_slice_set_tensor_float64")
     mask = (rng.random(20) < 0.5).astype(np.uint8)
-    lib.tensor_mask_set_scalar_float64(_p(d64), _p(_dev(mask)), ctypes.c_double(-1.0), ctypes.c_size_t(20))
+    dmask = _dev(mask)  # kept alive across the call
+    lib.tensor_mask_set_scalar_float64(_p(d64), _p(dmask), ctypes.c_double(-1.0), ctypes.c_size_t(20))
     zz = z.reshape(-1, order="F").copy()
     zz[mask.astype(bool)] = -1
     assert_exact(d64.cpu().numpy(), zz, "tensor_mask_set_scalar_float64")

@@ -83,6 +83,64 @@ def _rank_main(rank, world, port, x, q):
         dist.destroy_process_group()
 
 
+def _rank_main_packed(rank, world, port, x, q):
+    """The one-collective exchange: keys and rows in one int64 buffer, one
+    MAX all-reduce, then the host reference of acd_shard_finish."""
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        n2 = x.shape[2]
+        lo, hi = SH.shard_bounds(n2, rank, world)
+        z = oracle.gauss_chain(np.transpose(x[:, :, lo:hi], (2, 0, 1)), 0.5)
+        zl = z.reshape(z.shape[0], -1, order="F")
+        li = np.argmax(zl, axis=0)
+        keys = SH.pack_keys_np(zl[li, np.arange(zl.shape[1])], li + lo)
+        buf = torch.from_numpy(SH.pack_exchange_np(keys, _stats_row(z), rank, world))
+        dist.all_reduce(buf, op=dist.ReduceOp.MAX)
+        s, v, idx = SH.finish_exchange_np(buf.numpy(), keys.size, world)
+        q.put((rank, s, v, idx))
+    finally:
+        dist.destroy_process_group()
+
+
+def _run_ranks(target, world, x):
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=target, args=(r, world, port, x, q)) for r in range(world)]
+    for p in procs:
+        p.start()
+    out = [q.get(timeout=120) for _ in range(world)] if target is _rank_main_packed else [q.get(timeout=120)]
+    for p in procs:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    return out
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_one_max_all_reduce_carries_keys_and_rows(world):
+    rng = np.random.default_rng(3)
+    x = rng.standard_normal((16, 8, 24)).astype(np.float32)
+    x[:, :, 5] = x[:, :, 17]  # cross-shard ties
+    x[0, 0, :] = -0.0  # a statistics shift of -0.0 must survive the MAX
+    z = oracle.gauss_chain(np.transpose(x, (2, 0, 1)), 0.5)
+    es, ev = oracle.sum_var(z)
+    exp = oracle.arg_reduce("argmax", z, 0).reshape(-1, order="F")
+    for rank, s, v, idx in _run_ranks(_rank_main_packed, world, x):
+        assert abs(s - es) <= 1e-9 * abs(es) + 1e-9, rank
+        assert abs(v - ev) <= 1e-9 * abs(ev), rank
+        np.testing.assert_array_equal(idx, exp)
+
+
+def test_exchange_rows_survive_max_with_negative_and_zero_values():
+    rows = [[3.0, -0.0, -5.5, 2.0, -1e-300, 0.0], [2.0, -7.25, 0.5, 1.0, 0.0, -0.0]]
+    bufs = [SH.pack_exchange_np(np.zeros(3, dtype=np.int64), r, k, 2) for k, r in enumerate(rows)]
+    red = np.maximum(bufs[0], bufs[1])
+    got = red[3:].view(np.float64).reshape(2, -1)
+    np.testing.assert_array_equal(got.view(np.int64), np.asarray(rows, dtype=np.float64).view(np.int64))
+
+
 @pytest.mark.parametrize("world", [2])
 def test_two_gloo_ranks_reproduce_the_single_rank_result(world):
     rng = np.random.default_rng(2)

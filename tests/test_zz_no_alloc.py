@@ -2,9 +2,9 @@
 device memory (it needs no context and uses a static device array).
 
 Called through the C ABI and checked against acd_scan, the allocating entry
-point, on two calls in a row (the second call reuses the array the first one
-left behind).  This file is collected last so that a failure here leaves every
-other test already run.
+point, and against the oracle, on two calls in a row (the second call reuses
+the array the first one left behind).  This file is collected last so that a
+failure here leaves every other test already run.
 """
 import ctypes
 
@@ -14,6 +14,7 @@ import torch
 
 import acediar._lib as L
 import acediar.tensor as T
+import oracle
 
 pytestmark = pytest.mark.gpu
 
@@ -45,6 +46,26 @@ def test_noalloc_scan_matches_acd_scan_twice(acd, name, shape, axis):
             got = out.as_array()
             err = np.abs(got.astype(np.float64) - ref) - tol * np.abs(ref)
             assert np.all(err <= 0), "call %d %s: max excess %g" % (call, opname, err.max())
+            orc = oracle.scan(opname, xin.as_array(), a if axis is not None else None, threads=8)
+            err = np.abs(got.astype(np.float64) - orc) - tol * np.abs(orc)
+            assert np.all(err <= 0), "call %d %s vs oracle: max excess %g" % (call, opname, err.max())
+
+
+def test_noalloc_scan_two_lanes_near_its_limit(acd):
+    """Two interleaved float32 lanes: every tile costs 516 bytes of the
+    static array although only 2 of its 32 lanes are real, so 2 x 4,000,000
+    fits (15625 tiles, 8.06 MB) and 2 x 5,000,000 does not."""
+    lib = L.lib()
+    rng = np.random.default_rng(13)
+    x = rng.uniform(0, 1, (2, 4_000_000)).astype(np.float32)
+    t = acd.as_tensor(x, dtype="float")
+    out = T._alloc(t.shape, "float")
+    L.check(_noalloc(lib, 0, out, t, 1), "acd_scan_noalloc")
+    orc = oracle.scan("cumsum", x, 1, threads=2)
+    err = np.abs(out.as_array().astype(np.float64) - orc) - 1e-5 * np.abs(orc)
+    assert np.all(err <= 0), "max excess %g" % err.max()
+    big = L.make_desc(1, L.FLOAT32, (2, 5_000_000), (1, 2))
+    assert lib.acd_scan_noalloc(0, ctypes.byref(big), ctypes.byref(big), 1, None) == 8
 
 
 def test_noalloc_scan_rejects_beyond_its_static_scratch(acd):
