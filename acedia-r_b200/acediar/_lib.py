@@ -107,6 +107,7 @@ def _bind(lib):
         "acd_argmax_keys": ([vp, vp, dp, i32, i64, vp], i32),
         "acd_argmax_keys_decode": ([vp, dp, vp, i32, vp], i32),
         "acd_shard_exchange_init": ([vp, vp, i64, i32, vp], i32),
+        "acd_chain5_stats": ([vp, dp, dp, ctypes.POINTER(dp), vp, vp, vp], i32),
         "acd_shard_finish": ([vp, vp, i64, i32, dp, vp, i32, vp], i32),
         "acd_fused_stats_keys": ([vp, dp, dp, f64, vp, vp, i64, vp], i32),
         "acd_permute_fused_stats_keys": ([vp, dp, dp, dp, f64, vp, vp, i64, vp], i32),

@@ -809,6 +809,27 @@ def sum_var(x):
     return float(s.as_array()[0]), float(v.as_array()[0])
 
 
+def chain5_stats(a, b):
+    """The elementwise chain + reduction configuration in one kernel
+    (acd_chain5_stats): for float64 tensors a and b of one size, the tensors
+    a + b, a * b, exp(a), sigmoid(b), sqrt(a) (each bit-identical to the
+    operator), a float64[15] device tensor of their (sum, mean, var) and an
+    int64[1] device tensor holding which.max(a + b)."""
+    if a.dtype != "double" or b.dtype != "double" or a.size != b.size:
+        raise ValueError("chain5_stats: float64 tensors of one size required")
+    a = contiguous(a) if not a.is_contiguous() or a.offset else a
+    b = contiguous(b) if not b.is_contiguous() or b.offset else b
+    outs = [_alloc(a.shape, "double", a.device) for _ in range(5)]
+    stats = torch.empty(15, dtype=torch.float64, device=a.device)
+    which = torch.empty(1, dtype=torch.int64, device=a.device)
+    descs = [o.desc() for o in outs]
+    arr = (ctypes.POINTER(L.Desc) * 5)(*[ctypes.pointer(d) for d in descs])
+    L.check(L.lib().acd_chain5_stats(context(), ctypes.byref(a.desc()), ctypes.byref(b.desc()), arr,
+                                     ctypes.c_void_p(stats.data_ptr()), ctypes.c_void_p(which.data_ptr()), _stream()),
+            "chain5_stats")
+    return outs, stats, which
+
+
 def _arg(op, x, axis=None, keep_dims=False, one_based=True, index_dtype=None):
     if axis is None:
         idt = index_dtype or ("int32" if x.size < 2 ** 31 else "int64")

@@ -887,6 +887,158 @@ __global__ void __launch_bounds__(256) k_shard_finish(void *out, int32_t dt, lon
   }
 }
 
+// ---- the elementwise chain + reduction configuration in one pass -----------
+// For float64 a, b: c = a + b, d = a * b, e = exp(a), f = sigmoid(b),
+// g = sqrt(a), each rounded as its own operator (bit-identical to the
+// separate launches), and from the same registers the shifted moments of
+// each output (shift = its first element) and the first maximum of c.  One
+// launch replaces five elementwise kernels and sixteen reductions that would
+// re-read their inputs.  A thread adds only about n / (grid * 256) elements
+// (14 at n = 2^20) before the pairwise block and grid merges, so float64
+// moments keep the error near log2(n) ulp; double-double (VarAcc<double>)
+// would double the FP64 instructions of a kernel that is bound by them.
+struct Moments {
+  double k, s1, s2;
+  __device__ __forceinline__ void init() { k = 0.0; s1 = 0.0; s2 = 0.0; }
+  __device__ __forceinline__ void set_shift(double x) { k = x; }
+  __device__ __forceinline__ void add(double x, int64_t) {
+    const double d = x - k;
+    s1 += d;
+    s2 += d * d;
+  }
+  __device__ __forceinline__ void merge(const Moments &o) {
+    s1 += o.s1;
+    s2 += o.s2;
+  }
+  __device__ __forceinline__ double total(double n) const { return n * k + s1; }
+  __device__ __forceinline__ double var(double n) const {
+    if (n < 2.0) return (double)NAN;
+    const double v = (s2 - s1 * (s1 / n)) / (n - 1.0);
+    return v < 0.0 ? 0.0 : v;
+  }
+};
+
+struct Chain5Acc {
+  Moments v[5];
+  ArgAcc<double, true> am;
+  __device__ __forceinline__ void init() {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) v[k].init();
+    am.init();
+  }
+  __device__ __forceinline__ void merge(const Chain5Acc &o) {
+#pragma unroll
+    for (int k = 0; k < 5; ++k) v[k].merge(o.v[k]);
+    am.merge(o.am);
+  }
+};
+
+constexpr int kChain5Threads = 256;
+
+__device__ __forceinline__ void chain5_shifts(const double *a, const double *b, double K[5]) {
+  const double a0 = a[0], b0 = b[0];
+  K[0] = binary_apply<ACD_ADD, double, double>(a0, b0);
+  K[1] = binary_apply<ACD_MUL, double, double>(a0, b0);
+  K[2] = unary_apply<ACD_EXP, double>(a0);
+  K[3] = unary_apply<ACD_SIGMOID, double>(b0);
+  K[4] = unary_apply<ACD_SQRT, double>(a0);
+}
+
+__global__ void __launch_bounds__(kChain5Threads) k_chain5(const double *__restrict__ a, const double *__restrict__ b,
+                                                           double *__restrict__ c, double *__restrict__ d,
+                                                           double *__restrict__ e, double *__restrict__ f,
+                                                           double *__restrict__ g, int64_t n,
+                                                           Chain5Acc *__restrict__ partials, unsigned int *counter,
+                                                           double *__restrict__ stats, int64_t *__restrict__ which) {
+  __shared__ Chain5Acc smem[kChain5Threads / 32];
+  __shared__ int am_last;
+  double K[5];
+  chain5_shifts(a, b, K);
+  Chain5Acc acc;
+  acc.init();
+#pragma unroll
+  for (int k = 0; k < 5; ++k) acc.v[k].set_shift(K[k]);
+  const int64_t tid = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  constexpr int U = 4;  // elements in flight per thread
+  int64_t i = tid;
+  for (; i + (U - 1) * nth < n; i += U * nth) {
+    double xa[U], xb[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      xa[u] = a[i + u * nth];
+      xb[u] = b[i + u * nth];
+    }
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      const int64_t j = i + u * nth;
+      const double vc = binary_apply<ACD_ADD, double, double>(xa[u], xb[u]);
+      const double vd = binary_apply<ACD_MUL, double, double>(xa[u], xb[u]);
+      const double ve = unary_apply<ACD_EXP, double>(xa[u]);
+      const double vf = unary_apply<ACD_SIGMOID, double>(xb[u]);
+      const double vg = unary_apply<ACD_SQRT, double>(xa[u]);
+      c[j] = vc;
+      d[j] = vd;
+      e[j] = ve;
+      f[j] = vf;
+      g[j] = vg;
+      acc.v[0].add(vc, j);
+      acc.v[1].add(vd, j);
+      acc.v[2].add(ve, j);
+      acc.v[3].add(vf, j);
+      acc.v[4].add(vg, j);
+      acc.am.add(vc, j);
+    }
+  }
+  for (; i < n; i += nth) {
+    const double va = a[i], vb = b[i];
+    const double vc = binary_apply<ACD_ADD, double, double>(va, vb);
+    const double vd = binary_apply<ACD_MUL, double, double>(va, vb);
+    const double ve = unary_apply<ACD_EXP, double>(va);
+    const double vf = unary_apply<ACD_SIGMOID, double>(vb);
+    const double vg = unary_apply<ACD_SQRT, double>(va);
+    c[i] = vc;
+    d[i] = vd;
+    e[i] = ve;
+    f[i] = vf;
+    g[i] = vg;
+    acc.v[0].add(vc, i);
+    acc.v[1].add(vd, i);
+    acc.v[2].add(ve, i);
+    acc.v[3].add(vf, i);
+    acc.v[4].add(vg, i);
+    acc.am.add(vc, i);
+  }
+  // grid merge: per-CTA partials, the last CTA merges them in index order
+  block_reduce(acc, smem);
+  if (threadIdx.x == 0) {
+    partials[blockIdx.x] = acc;
+    __threadfence();
+    am_last = (atomicAdd(counter, 1u) == gridDim.x - 1);
+  }
+  __syncthreads();
+  if (!am_last) return;
+  __threadfence();
+  Chain5Acc fin;
+  fin.init();
+#pragma unroll
+  for (int k = 0; k < 5; ++k) fin.v[k].set_shift(K[k]);
+  for (int q = threadIdx.x; q < (int)gridDim.x; q += blockDim.x) fin.merge(load_cg(partials + q));
+  block_reduce(fin, smem);
+  if (threadIdx.x == 0) {
+    const double nn = (double)n;
+#pragma unroll
+    for (int k = 0; k < 5; ++k) {
+      const double tot = fin.v[k].total(nn);
+      stats[3 * k] = tot;
+      stats[3 * k + 1] = tot / nn;
+      stats[3 * k + 2] = fin.v[k].var(nn);
+    }
+    which[0] = fin.am.i == LLONG_MAX ? -1 : fin.am.i + 1;
+    *counter = 0u;
+  }
+}
+
 __global__ void k_shard_rows_init(long long *rows, int64_t n) {
   for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n; j += (int64_t)gridDim.x * blockDim.x)
     rows[j] = LLONG_MIN;
@@ -1076,6 +1228,38 @@ acd_status acd_argmax_keys_decode(acd_ctx *ctx, const acd_desc *out_index, const
   const int grid = grid_for(ctx, n, 256, 4);
   k_keys_decode<<<grid, 256, 0, s>>>(desc_ptr(out_index), out_index->dtype, reinterpret_cast<const long long *>(keys),
                                      n, one_based ? 1 : 0);
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_chain5_stats(acd_ctx *ctx, const acd_desc *a, const acd_desc *b, const acd_desc *const *outs,
+                            double *stats, int64_t *which_max, acd_stream stream) {
+  if (!ctx || !a || !b || !outs || !stats || !which_max) return fail(ACD_ERR_INVALID, "acd_chain5_stats: null argument");
+  ACD_TRY(check_desc(a, "a"));
+  ACD_TRY(check_desc(b, "b"));
+  const int64_t n = desc_numel(a);
+  if (a->dtype != ACD_FLOAT64 || b->dtype != ACD_FLOAT64)
+    return fail(ACD_ERR_DTYPE, "acd_chain5_stats: float64 inputs required");
+  if (desc_numel(b) != n || !desc_is_contiguous(a) || !desc_is_contiguous(b))
+    return fail(ACD_ERR_SHAPE, "acd_chain5_stats: a and b must be contiguous with one element count");
+  if (n < 1) return fail(ACD_ERR_UNSUPPORTED, "acd_chain5_stats: empty input");
+  double *o[5];
+  for (int k = 0; k < 5; ++k) {
+    if (!outs[k]) return fail(ACD_ERR_INVALID, "acd_chain5_stats: null output %d", k);
+    ACD_TRY(check_desc(outs[k], "out"));
+    if (outs[k]->dtype != ACD_FLOAT64 || desc_numel(outs[k]) != n || !desc_is_contiguous(outs[k]))
+      return fail(ACD_ERR_SHAPE, "acd_chain5_stats: output %d must be contiguous float64 of the input size", k);
+    o[k] = reinterpret_cast<double *>(desc_ptr(outs[k]));
+  }
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int grid = persistent_grid(ctx, k_chain5, kChain5Threads, 0, (n + 4 * kChain5Threads - 1) / (4 * kChain5Threads));
+  void *scratch;
+  ACD_TRY(get_scratch(ctx, align_up(sizeof(Chain5Acc) * grid, 256), s, &scratch));
+  k_chain5<<<grid, kChain5Threads, 0, s>>>(reinterpret_cast<const double *>(desc_ptr(a)),
+                                           reinterpret_cast<const double *>(desc_ptr(b)), o[0], o[1], o[2], o[3], o[4], n,
+                                           static_cast<Chain5Acc *>(scratch), &ctx->control->counters[1], stats,
+                                           which_max);
   ACD_CUDA(cudaGetLastError());
   return ACD_OK;
 }

@@ -526,7 +526,7 @@ __device__ __forceinline__ void merge_ms(double &M, double &S, double m, double 
 }
 
 template <typename T, int U>
-__global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
+__global__ void __launch_bounds__(256, sizeof(T) == 4 ? 3 : 2) k_softmax_l2(SoftL2Args a) {
   constexpr int VL = 16 / sizeof(T);
   constexpr int GW = 32 * VL;
   using P = Vec<T, 2>;  // (m, s) or (M, 1/S)
@@ -551,6 +551,11 @@ __global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
     const int64_t g = is_a ? blk : blk - a.lag;
     const int64_t c = is_a ? slot : slot - a.nchunks;
     __syncthreads();  // s_ticket, s_last and red_* reuse
+    // the next ticket is taken now, so its round trip overlaps this item (a
+    // CTA holds at most one ticket it has not started; the smallest
+    // unfinished ticket is always some CTA's current item, so work proceeds)
+    unsigned int next = 0u;
+    if (threadIdx.x == 0) next = atomicAdd(ticket, 1u);
     if (g >= 0 && g < a.ng) {
       const int64_t o = g / a.lgroups, lg = g % a.lgroups;
       const int64_t l0 = lg * GW + (int64_t)lane32 * VL;  // first lane of this thread
@@ -645,7 +650,14 @@ __global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
           if (threadIdx.x == 0) st_release_u32(&ready[g], 1u);
         }
       } else {
-        // ---- B: wait for the group's statistics, then write
+        // ---- B: the first loads go out before the wait for the group's
+        // statistics (they do not depend on them), then write
+        Vec<T, VL> x[U];
+        const bool first = lane_ok && r0 + U - 1 < r1;
+        if (first) {
+#pragma unroll
+          for (int u = 0; u < U; ++u) x[u] = ld_hint(in + (r0 + u) * a.sr, drop);
+        }
         if (threadIdx.x == 0) {
           if (ld_acquire_u32(&ready[g]) == 0u) {
             const uint64_t t0 = global_timer_ns();
@@ -669,8 +681,17 @@ __global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
         T *out = static_cast<T *>(a.out) + o * a.oo + l0;
         if (lane_ok) {
           int64_t r = r0;
+          if (first) {
+#pragma unroll
+            for (int u = 0; u < U; ++u) {
+              Vec<T, VL> y;
+#pragma unroll
+              for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x[u].v[k] - M[k]) * inv[k];
+              st_hint(out + (r0 + u) * a.orr, y, drop);
+            }
+            r += U;
+          }
           for (; r + U - 1 < r1; r += U) {
-            Vec<T, VL> x[U];
 #pragma unroll
             for (int u = 0; u < U; ++u) x[u] = ld_hint(in + (r + u) * a.sr, drop);
 #pragma unroll
@@ -698,7 +719,7 @@ __global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
         }
       }
     }
-    if (threadIdx.x == 0) s_ticket = (int64_t)atomicAdd(ticket, 1u);
+    if (threadIdx.x == 0) s_ticket = (int64_t)next;
     __syncthreads();
     t = s_ticket;
   }
@@ -708,9 +729,14 @@ __global__ void __launch_bounds__(256) k_softmax_l2(SoftL2Args a) {
   }
 }
 
-// Tuning of k_softmax_l2: steps per chunk, CTAs per SM and the lag in
-// groups.  Items of 128 KB; the lag puts about 24 MB of input between a
-// group's A and B items.
+// Tuning of k_softmax_l2: items of 128 KB and a lag of about 96 MB of input
+// between a group's A and B items.  Sweeps over 32-512 KB items and 8-96 MB
+// lags on 65536x4096 float32: 32 KB / 8 MB took 1.9 ms (per-item latency:
+// ticket, flag and statistics round trips), 128 KB / 96 MB 0.56 ms.  A
+// shorter lag keeps more of the re-read in L2 but leaves B items waiting on
+// groups whose A items are still in flight (444 CTAs x 128 KB = 57 MB are
+// in flight at once); at 48 MB ncu counted 1.79 GB of DRAM reads for the
+// 1.07 GB input, i.e. a third of the re-read hit L2.
 template <typename T>
 static acd_status launch_softmax_l2(acd_ctx *ctx, SoftArgs sa, cudaStream_t s) {
   constexpr int VL = 16 / sizeof(T);
@@ -733,7 +759,7 @@ static acd_status launch_softmax_l2(acd_ctx *ctx, SoftArgs sa, cudaStream_t s) {
   a.chunk = chunk;
   a.nchunks = (sa.R + chunk - 1) / chunk;
   const int64_t group_bytes = a.nchunks * chunk * row_bytes;
-  a.lag = (24ll << 20) / group_bytes;
+  a.lag = (96ll << 20) / group_bytes;
   if (a.lag < 1) a.lag = 1;
   if (a.lag > a.ng) a.lag = a.ng;
   a.total = (a.ng + a.lag) * 2 * a.nchunks;
@@ -1182,8 +1208,14 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
   // contiguous lanes: the wide two-pass kernels when there are at least 256
   // vectors of lanes (measured faster than the cluster kernel on
   // 65536x4096 float32: 0.60 vs 0.77 ms), else the single-read cluster kernel
-  if (wide)
+  // the single-launch kernel needs enough lane groups (512-byte columns of
+  // lanes) to keep the pipeline of statistics and apply items full: with 16
+  // groups (1024x32768 float64) the two-pass kernels win, 0.18 vs 0.30 ms
+  const int64_t lane_groups = (a.L + 32 * VL - 1) / (32 * VL) * a.O;
+  if (wide && lane_groups >= 64)
     st = f32 ? launch_softmax_l2<float>(ctx, a, s) : launch_softmax_l2<double>(ctx, a, s);
+  else if (wide)
+    st = f32 ? launch_softmax_wide<float>(ctx, a, s) : launch_softmax_wide<double>(ctx, a, s);
   else if (f32 ? launch_softmax_tma<float>(ctx, a, s) : launch_softmax_tma<double>(ctx, a, s))
     st = ACD_OK;
   else if (a.L == 1)

@@ -307,6 +307,10 @@ def config_ops(workload, peak):
         torch.cuda.synchronize()
         ops.append(_op("whole config (CUDA graph)", graph.replay, total_bytes, peak, reps=50,
                        note="launch overhead removed; arrays stay in L2"))
+        # one kernel: a and b read once, c..g written once, 15 statistics and
+        # which.max from the same registers (56 MiB moved)
+        ops.append(_op("whole config (one kernel, acd_chain5_stats)", lambda: Tm.chain5_stats(ta, tb), 7 * B, peak,
+                       graph=True, reps=20, note="algorithmic bytes: a, b read + c..g written"))
         workload = "elementwise chain + reductions, float64 n=2^20"
         unit_elems = n
     elif workload == "c2":

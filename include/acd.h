@@ -305,6 +305,18 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
  * the shared array.  This entry point has no counterpart in the reference. */
 acd_status acd_scan_noalloc(int32_t op, const acd_desc *out, const acd_desc *in, int32_t axis, acd_stream stream);
 
+/* The elementwise chain + reduction configuration in one pass.  For float64
+ * contiguous a and b of n elements, writes outs[0..4] = a + b, a * b,
+ * exp(a), sigmoid(b), sqrt(a) (each bit-identical to acd_binary / acd_unary
+ * of that operator) and, from the same registers, stats[3k], stats[3k+1],
+ * stats[3k+2] = sum, mean, sample variance of outs[k] (device float64[15])
+ * and which_max[0] = which.max(outs[0]) (1-based, first index; device
+ * int64[1]).  Replaces five elementwise calls and sixteen reductions
+ * (R's `+`, `*`, exp, sigmoid, sqrt, then sum/mean/var and which.max,
+ * R/gpuTensor.R; src/kernels/tensor_ops.cu:785-880); a and b are read once. */
+acd_status acd_chain5_stats(acd_ctx *ctx, const acd_desc *a, const acd_desc *b, const acd_desc *const *outs,
+                            double *stats, int64_t *which_max, acd_stream stream);
+
 /* ---- sharded partials (multi-GPU global sum/var and argmax) ------------- */
 /* Writes this shard's partial statistics of all elements of `in` to the
  * device array `stats` (float64[4]: n, shift, sum(x-shift), sum((x-shift)^2)),

@@ -4,7 +4,10 @@
 # it to pin the CPU oracle against the reference's own results on small
 # inputs.  Needs the reference sources (present only on the build machine);
 # the built library travels with the repository snapshot.
-REF ?= /root/reference/src
+# REF: the reference checkout's src/ directory (make REF=...); by default
+# $(ACEDIAR_REF)/src, with ACEDIAR_REF defaulting to the build machine's copy
+ACEDIAR_REF ?= /root/reference
+REF ?= $(ACEDIAR_REF)/src
 NVCC ?= nvcc
 OUT := _ref/libacediar_ref.so
 

@@ -71,6 +71,18 @@ def test_c1_chain_and_statistics(acd):
         assert_rel(acd.mean(t), oracle.reduce("mean", h), F64, "C1 mean(%s)" % k)
         assert_rel(acd.var(t), oracle.reduce("var", h), F64, "C1 var(%s)" % k)
     assert acd.which_max(got["c"]) == oracle.arg_reduce("argmax", _host(got["c"]))
+    # the whole configuration as one kernel: the same five tensors bit for bit,
+    # the 15 statistics against the oracle, which.max exact
+    import acediar.tensor as Tm
+    outs, stats, which = Tm.chain5_stats(a, b)
+    st = stats.cpu().numpy()
+    for k, o in zip("cdefg", outs):
+        assert_exact(_host(o), _host(got[k]), "C1 fused %s vs the operator" % k)
+        h = _host(o)
+        assert_rel(st["cdefg".index(k) * 3], oracle.reduce("sum", h), F64, "C1 fused sum(%s)" % k)
+        assert_rel(st["cdefg".index(k) * 3 + 1], oracle.reduce("mean", h), F64, "C1 fused mean(%s)" % k)
+        assert_rel(st["cdefg".index(k) * 3 + 2], oracle.reduce("var", h), F64, "C1 fused var(%s)" % k)
+    assert int(which.item()) == oracle.arg_reduce("argmax", _host(got["c"]))
 
 
 # ---------------------------------------------------------------------------
