@@ -458,12 +458,17 @@ def main():
     xp_view = acediar.permute_view(x, [3, 1, 2])
     y = _alloc((n2l, N0, N1), "float", dev)
     z = _alloc((n2l, N0, N1), "float", dev)
-    # one int64 exchange buffer: the argmax keys, then one statistics row per
-    # rank; a single MAX all-reduce carries both (acediar.sharded)
+    # two int64 exchange buffers (steps alternate): the argmax keys, then one
+    # statistics row per rank; a single MAX all-reduce carries both
+    # (acediar.sharded).  Step k's exchange and finish run on a side stream
+    # under step k+1's transpose; step k+2 reuses the buffer once step k's
+    # finish has read it.
     nkeys = N0 * N1
-    xbuf = SH.exchange_buffer(nkeys, world, dev)
-    row_ptr = SH.row_slot(xbuf, nkeys, rank)
-    keys_ptr = ctypes.c_void_p(xbuf.data_ptr())
+    xbufs = [SH.exchange_buffer(nkeys, world, dev) for _ in range(2)]
+    row_ptrs = [SH.row_slot(b, nkeys, rank) for b in xbufs]
+    keys_ptrs = [ctypes.c_void_p(b.data_ptr()) for b in xbufs]
+    side = torch.cuda.Stream(device=dev)
+    finished = [None, None]  # events: step's finish has read the buffer
     sum_var = torch.empty(2, dtype=torch.float64, device=dev)
     sv_ptr = ctypes.c_void_p(sum_var.data_ptr())
     idx = _alloc((N0, N1), "int32", dev)
@@ -476,29 +481,43 @@ def main():
     def k_transpose(s, dx=None):
         L.check(lib.acd_copy(ctx, pref(d_y), pref(dx if dx is not None else d_xp), s), "copy")
 
-    def k_chain_stats_keys(s):
+    def k_chain_stats_keys(s, b=0):
         # z = y*0.5 + exp(-y^2), with this shard's statistics row of z and the
         # argmax keys of z along axis 1 from the same pass (z is not re-read),
-        # written straight into the exchange buffer
-        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5), row_ptr, keys_ptr, lo, s),
-                "fused_stats_keys")
+        # written straight into exchange buffer b
+        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5), row_ptrs[b], keys_ptrs[b],
+                                         lo, s), "fused_stats_keys")
 
-    def exchange():
+    def exchange(b=0, async_op=False):
         if world > 1:
-            dist.all_reduce(xbuf, op=dist.ReduceOp.MAX)
+            return dist.all_reduce(xbufs[b], op=dist.ReduceOp.MAX, async_op=async_op)
+        return None
 
-    def k_finish(s):
+    def k_finish(s, b=0):
         # argmax indices, and the rows merged in rank order into (sum, var)
-        L.check(lib.acd_shard_finish(ctx, keys_ptr, nkeys, world, pref(d_idx), sv_ptr, 1, s), "shard_finish")
+        L.check(lib.acd_shard_finish(ctx, keys_ptrs[b], nkeys, world, pref(d_idx), sv_ptr, 1, s), "shard_finish")
 
-    def step(dx=None, input_read=None):
+    def step(k, dx=None, input_read=None):
         s = stream()
+        b = k % 2
         k_transpose(s, dx)
         if input_read is not None:
             input_read.record()  # the transpose is the only reader of the input
-        k_chain_stats_keys(s)
-        exchange()
-        k_finish(stream())
+        if finished[b] is not None:
+            torch.cuda.current_stream().wait_event(finished[b])  # step k-2's finish has read buffer b
+        k_chain_stats_keys(s, b)
+        work = exchange(b, async_op=True)
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            if work is not None:
+                work.wait()  # the side stream waits for the collective
+            k_finish(ctypes.c_void_p(side.cuda_stream), b)
+            ev = torch.cuda.Event()
+            ev.record(side)
+            finished[b] = ev
+
+    def join():
+        torch.cuda.current_stream().wait_stream(side)
 
     LAUNCHES_PER_STEP = 3  # transpose, chain with statistics and keys, exchange finish
 
@@ -508,8 +527,9 @@ def main():
             dist.barrier(device_ids=[local])
         torch.cuda.synchronize()
 
-    for _ in range(max(3, a.warmup)):
-        step()
+    for k in range(max(3, a.warmup)):
+        step(k)
+    join()
     barrier()
     clocks = Clocks([local]) if rank == 0 else None
     if clocks:
@@ -517,8 +537,9 @@ def main():
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     barrier()
     e0.record()
-    for _ in range(a.steps):
-        step()
+    for k in range(a.steps):
+        step(k)
+    join()  # the last step's exchange and finish are inside the timed region
     e1.record()
     barrier()
     ms = e0.elapsed_time(e1) / a.steps
@@ -613,9 +634,11 @@ def main():
                 issue_copy(k + 1)
             b = k % 2
             torch.cuda.current_stream().wait_event(copied[b])
-            step(bufs[b][1], read[b])
-            res_h.copy_(sum_var, non_blocking=True)
-            idx_h.copy_(idx.storage[:N0 * N1], non_blocking=True)
+            step(k, bufs[b][1], read[b])
+            with torch.cuda.stream(side):  # the results of step k, after its finish
+                res_h.copy_(sum_var, non_blocking=True)
+                idx_h.copy_(idx.storage[:N0 * N1], non_blocking=True)
+        join()
         f1.record()
         barrier()
         ems = f0.elapsed_time(f1) / a.e2e_steps
@@ -639,7 +662,7 @@ def main():
     # ---- the other configurations' per-op reports (one GPU)
     per_config = None
     if world == 1 and not a.no_per_config:
-        del x, y, z, xbuf, xp_view
+        del x, y, z, xbufs, xp_view
         torch.cuda.synchronize()
         torch.cuda.empty_cache()
         per_config = per_config_block(peak)
