@@ -778,304 +778,6 @@ static acd_status launch_softmax_l2(acd_ctx *ctx, SoftArgs sa, cudaStream_t s) {
   return ACD_OK;
 }
 
-// ---- one HBM read, items held in shared memory ------------------------------
-// The items of k_softmax_l2 (lane group g of GW lanes, chunk c of CH steps),
-// but a CTA keeps each item it claims in its own shared memory until the
-// item is written: one CTA per SM with three item buffers.  Per round a CTA
-//   1. claims the next item (global ticket) and starts its TMA load into the
-//      free buffer;
-//   2. computes the statistics of its current item (loaded a round earlier)
-//      and publishes them; the CTA completing a group merges the group;
-//   3. applies its previous item: waits until the previous item's group is
-//      flagged, then writes exp(x - M) * (1/S) from shared memory.
-// HBM sees each input byte once and each output byte once, and the load of
-// step 1 is in flight during steps 2 and 3.  A CTA never waits on a group
-// while it holds an item of that group whose statistics it has not
-// published: when the claimed item belongs to the group being waited for, its
-// statistics are computed first.  So the lowest group anybody waits for has
-// all its items published or in running CTAs that do not wait on it, and
-// every wait ends (bounded anyway: 1 s by %globaltimer, status code 4; TMA
-// waits likewise, status 3).
-struct SoftPipeArgs {
-  int64_t L, R, O;
-  int64_t lgroups, ng, nchunks;
-  int CH;                   // steps per item (<= 256, a multiple of 8)
-  int64_t total;            // ng * nchunks tickets
-  int64_t oo, orr;          // output strides (lanes contiguous)
-  void *out;
-  unsigned int *cnt;        // [3 * ng + 2]
-  void *part, *stat;        // as SoftL2Args
-  Control *control;
-};
-
-template <typename T>
-__global__ void __launch_bounds__(256, 1) k_softmax_pipe(const __grid_constant__ CUtensorMap map_in, SoftPipeArgs a) {
-  constexpr int VL = 16 / sizeof(T);
-  constexpr int GW = 32 * VL;
-  constexpr int NB = 3;
-  using P = Vec<T, 2>;
-  extern __shared__ unsigned char smem_raw[];
-  T *bufs = reinterpret_cast<T *>((reinterpret_cast<uintptr_t>(smem_raw) + 127) & ~static_cast<uintptr_t>(127));
-  __shared__ uint64_t bar[NB];
-  __shared__ double red_m[8][GW], red_s[8][GW];
-  __shared__ int64_t s_ticket;
-  __shared__ int s_last, s_fault;
-  const int tid = threadIdx.x, warp = tid / 32, lane32 = tid % 32;
-  const size_t buf_elems = (size_t)a.CH * GW;
-  P *part = static_cast<P *>(a.part);
-  P *stat = static_cast<P *>(a.stat);
-  unsigned int *cntA = a.cnt, *ready = a.cnt + a.ng, *cntB = a.cnt + 2 * a.ng;
-  unsigned int *ticket = a.cnt + 3 * a.ng, *done = ticket + 1;
-  if (tid == 0) {
-    for (int b = 0; b < NB; ++b) mbar_init(&bar[b], 1);
-    mbar_init_fence();
-    s_fault = 0;
-  }
-  __syncthreads();
-
-  // item slots: ticket (-1 = none), buffer, statistics published, load phase
-  int64_t it_t[3] = {-1, -1, -1};  // prev, cur, next
-  int it_b[3] = {0, 0, 0};
-  bool it_a[3] = {false, false, false};
-  uint32_t phase[NB] = {0u, 0u, 0u};
-  bool busy[NB] = {false, false, false};
-  bool pending[NB] = {false, false, false};  // a load into the buffer not yet seen landed
-
-  auto group_of = [&](int64_t t) { return t / a.nchunks; };
-  // after an expired wait the CTA takes no further items, so a fault costs at
-  // most a few bounded waits
-  auto claim = [&]() -> int64_t {
-    if (tid == 0) s_ticket = (int64_t)atomicAdd(ticket, 1u);
-    __syncthreads();
-    const int64_t t = s_ticket;
-    const int fault = s_fault;
-    __syncthreads();
-    return (t < a.total && !fault) ? t : -1;
-  };
-  auto start_load = [&](int64_t t, int b) {
-    pending[b] = true;
-    if (tid == 0) {
-      const int64_t g = t / a.nchunks, c = t % a.nchunks;
-      const int64_t o = g / a.lgroups, lg = g % a.lgroups;
-      mbar_arrive_expect_tx(&bar[b], (uint32_t)(buf_elems * sizeof(T)));
-      tma_load_3d(bufs + (size_t)b * buf_elems, &map_in, &bar[b], (int)(lg * GW), (int)(c * a.CH), (int)o);
-    }
-  };
-  // statistics of item t in buffer b (every thread waits for its load)
-  auto stats_of = [&](int64_t t, int b) {
-    if (!mbar_wait_bounded(&bar[b], phase[b], 1000000000ull)) {
-      raise_status(a.control, 3, (int32_t)blockIdx.x);
-      s_fault = 1;  // the load may still land: waited for again before exit
-    } else {
-      pending[b] = false;
-    }
-    __syncthreads();
-    phase[b] ^= 1u;
-    const int64_t g = t / a.nchunks, c = t % a.nchunks;
-    int nsteps = (int)(a.R - c * a.CH);
-    if (nsteps > a.CH) nsteps = a.CH;
-    const Vec<T, VL> *tv = reinterpret_cast<const Vec<T, VL> *>(bufs + (size_t)b * buf_elems) + lane32;
-    T m[VL], sm[VL];
-#pragma unroll
-    for (int k = 0; k < VL; ++k) {
-      m[k] = lowest_of<T>();
-      sm[k] = T(0);
-    }
-    for (int r = warp; r < nsteps; r += 8) {
-      const Vec<T, VL> x = tv[(size_t)r * 32];
-#pragma unroll
-      for (int k = 0; k < VL; ++k) {
-        const T mn = m_max(m[k], x.v[k]);
-        if (mn == lowest_of<T>()) continue;
-        const T acc = (m[k] == lowest_of<T>()) ? T(0) : sm[k] * m_exp(m[k] - mn);
-        sm[k] = acc + m_exp(x.v[k] - mn);
-        m[k] = mn;
-      }
-    }
-#pragma unroll
-    for (int k = 0; k < VL; ++k) {
-      red_m[warp][lane32 * VL + k] = m[k] == lowest_of<T>() ? -INFINITY : (double)m[k];
-      red_s[warp][lane32 * VL + k] = (double)sm[k];
-    }
-    __syncthreads();
-    P *dst = part + (g * a.nchunks + c) * GW;
-    for (int i = tid; i < GW; i += blockDim.x) {
-      double M = -INFINITY, S = 0.0;
-      for (int w = 0; w < 8; ++w) merge_ms(M, S, red_m[w][i], red_s[w][i]);
-      P pr;
-      pr.v[0] = M == -INFINITY ? lowest_of<T>() : (T)M;
-      pr.v[1] = (T)S;
-      dst[i] = pr;
-    }
-    __threadfence();
-    __syncthreads();
-    if (tid == 0) s_last = (atomicAdd(&cntA[g], 1u) == (unsigned int)(a.nchunks - 1));
-    __syncthreads();
-    if (s_last) {
-      __threadfence();
-      for (int i = tid; i < GW; i += blockDim.x) {
-        const P *src = part + g * a.nchunks * GW + i;
-        double M = -INFINITY;
-        for (int64_t q = 0; q < a.nchunks; ++q) {
-          const P v = ld_pair_cg(src + q * GW);
-          if (v.v[0] != lowest_of<T>()) M = fmax(M, (double)v.v[0]);
-        }
-        double S = 0.0;
-        if (M != -INFINITY)
-          for (int64_t q = 0; q < a.nchunks; ++q) {
-            const P v = ld_pair_cg(src + q * GW);
-            if (v.v[0] != lowest_of<T>()) S += (double)v.v[1] * exp((double)v.v[0] - M);
-          }
-        P st;
-        st.v[0] = M == -INFINITY ? lowest_of<T>() : (T)M;
-        st.v[1] = (T)(1.0 / S);
-        stat[g * GW + i] = st;
-      }
-      __threadfence();
-      __syncthreads();
-      if (tid == 0) st_release_u32(&ready[g], 1u);
-    }
-    __syncthreads();  // red_* and s_last reuse
-  };
-  // apply item t from buffer b (waits for its group)
-  auto apply = [&](int64_t t, int b) {
-    const int64_t g = t / a.nchunks, c = t % a.nchunks;
-    if (tid == 0 && ld_acquire_u32(&ready[g]) == 0u) {
-      const uint64_t t0 = global_timer_ns();
-      while (ld_acquire_u32(&ready[g]) == 0u) {
-        if (global_timer_ns() - t0 > 1000000000ull) {
-          raise_status(a.control, 4, (int32_t)(g & 0x7fffffff));
-          s_fault = 1;
-          break;
-        }
-        __nanosleep(100);
-      }
-    }
-    __syncthreads();
-    const int64_t o = g / a.lgroups, lg = g % a.lgroups;
-    const int64_t l0 = lg * GW + (int64_t)lane32 * VL;
-    const bool lane_ok = l0 < a.L;
-    int nsteps = (int)(a.R - c * a.CH);
-    if (nsteps > a.CH) nsteps = a.CH;
-    T M[VL], inv[VL];
-#pragma unroll
-    for (int k = 0; k < VL; ++k) {
-      const P st = lane_ok ? ld_pair_cg(stat + g * GW + lane32 * VL + k) : P{};
-      M[k] = st.v[0];
-      inv[k] = st.v[1];
-    }
-    if (lane_ok) {
-      const Vec<T, VL> *tv = reinterpret_cast<const Vec<T, VL> *>(bufs + (size_t)b * buf_elems) + lane32;
-      T *out = static_cast<T *>(a.out) + o * a.oo + l0 + c * a.CH * a.orr;
-      for (int r = warp; r < nsteps; r += 8) {
-        const Vec<T, VL> x = tv[(size_t)r * 32];
-        Vec<T, VL> y;
-#pragma unroll
-        for (int k = 0; k < VL; ++k) y.v[k] = m_exp(x.v[k] - M[k]) * inv[k];
-        *reinterpret_cast<Vec<T, VL> *>(out + (int64_t)r * a.orr) = y;
-      }
-    }
-    __syncthreads();  // every thread has read the buffer and the statistics
-    if (tid == 0 && atomicAdd(&cntB[g], 1u) == (unsigned int)(a.nchunks - 1)) {
-      cntA[g] = 0u;
-      ready[g] = 0u;
-      cntB[g] = 0u;
-    }
-  };
-  auto free_buf = [&]() {
-    for (int b = 0; b < NB; ++b)
-      if (!busy[b]) return b;
-    return 0;  // unreachable: at most two items are held when a third is claimed
-  };
-
-  // rounds: claim next, statistics of cur, apply prev
-  while (true) {
-    it_t[2] = claim();
-    if (it_t[2] >= 0) {
-      it_b[2] = free_buf();
-      busy[it_b[2]] = true;
-      it_a[2] = false;
-      start_load(it_t[2], it_b[2]);
-    }
-    if (it_t[1] >= 0 && !it_a[1]) {
-      stats_of(it_t[1], it_b[1]);
-      it_a[1] = true;
-    }
-    if (it_t[0] >= 0) {
-      // never wait on a group while holding an unpublished item of it
-      if (it_t[2] >= 0 && !it_a[2] && group_of(it_t[2]) == group_of(it_t[0])) {
-        stats_of(it_t[2], it_b[2]);
-        it_a[2] = true;
-      }
-      apply(it_t[0], it_b[0]);
-      busy[it_b[0]] = false;
-    }
-    if (it_t[0] < 0 && it_t[1] < 0 && it_t[2] < 0) break;
-    it_t[0] = it_t[1];
-    it_b[0] = it_b[1];
-    it_a[0] = it_a[1];
-    it_t[1] = it_t[2];
-    it_b[1] = it_b[2];
-    it_a[1] = it_a[2];
-    it_t[2] = -1;
-  }
-  // a load whose wait expired must land before the CTA's shared memory goes
-  for (int b = 0; b < NB; ++b)
-    if (pending[b] && tid == 0) mbar_wait_bounded(&bar[b], phase[b] ^ 1u, 1000000000ull);
-  if (tid == 0 && atomicAdd(done, 1u) == gridDim.x - 1) {
-    *ticket = 0u;
-    *done = 0u;
-  }
-}
-
-template <typename T>
-static bool launch_softmax_pipe(acd_ctx *ctx, const SoftArgs &sa, cudaStream_t s) {
-  constexpr int VL = 16 / sizeof(T);
-  constexpr int64_t GW = 32 * VL;
-  if (sa.sl != 1 || sa.ol != 1 || sa.L % VL) return false;
-  if ((sa.sr * (int64_t)sizeof(T)) % 16 || (sa.orr * (int64_t)sizeof(T)) % 16) return false;
-  if (sa.O > 1 && ((sa.so * (int64_t)sizeof(T)) % 16 || (sa.oo * (int64_t)sizeof(T)) % 16)) return false;
-  if ((reinterpret_cast<uintptr_t>(sa.in) | reinterpret_cast<uintptr_t>(sa.out)) & 15) return false;
-  if (sa.L >= (1ll << 31) || sa.R >= (1ll << 31) || sa.O >= (1ll << 31)) return false;
-  SoftPipeArgs a{};
-  a.L = sa.L;
-  a.R = sa.R;
-  a.O = sa.O;
-  a.lgroups = (sa.L + GW - 1) / GW;
-  a.ng = a.lgroups * sa.O;
-  a.CH = 128;  // 64 KB items for float32 and float64 (512-byte rows)
-  if (sa.R < a.CH) a.CH = (int)((sa.R + 7) / 8 * 8);
-  a.nchunks = (sa.R + a.CH - 1) / a.CH;
-  a.total = a.ng * a.nchunks;
-  if (a.total >= (1ll << 31)) return false;
-  a.oo = sa.oo;
-  a.orr = sa.orr;
-  a.out = sa.out;
-  a.control = ctx->control;
-  if (get_counters(ctx, (size_t)(3 * a.ng + 2), s, &a.cnt) != ACD_OK) return false;
-  const size_t pbytes = sizeof(T) * 2 * (size_t)(a.ng * a.nchunks * GW);
-  const size_t sbytes = sizeof(T) * 2 * (size_t)(a.ng * GW);
-  void *scratch;
-  if (get_scratch(ctx, pbytes + sbytes, s, &scratch) != ACD_OK) return false;
-  a.part = scratch;
-  a.stat = static_cast<char *>(scratch) + pbytes;
-  CUtensorMap mi;
-  const int64_t d[3] = {sa.L, sa.R, sa.O};
-  const int64_t si[2] = {sa.sr, sa.O > 1 ? sa.so : sa.sr * sa.R};
-  const uint32_t box[3] = {(uint32_t)GW, (uint32_t)a.CH, 1};
-  if (!encode_tensor_map_3d(&mi, sa.in, (int)sizeof(T), d, si, box, false, true)) return false;
-  const size_t dyn = 3 * (size_t)a.CH * GW * sizeof(T) + 128;
-  auto kern = k_softmax_pipe<T>;
-  if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)dyn) != cudaSuccess) {
-    cudaGetLastError();
-    return false;
-  }
-  int grid = ctx->sm_count;
-  if ((int64_t)grid > a.total) grid = (int)a.total;
-  kern<<<grid, 256, dyn, s>>>(mi, a);
-  return cudaGetLastError() == cudaSuccess;
-}
-
 // ---- one read through TMA: a cluster holds a lane block's whole row ---------
 // For lanes contiguous in memory (the row softmax of a column-major matrix)
 // whose R steps x 128 bytes fit the shared memory of a cluster of up to 16
@@ -1510,9 +1212,7 @@ acd_status acd_softmax(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, in
   // lanes) to keep the pipeline of statistics and apply items full: with 16
   // groups (1024x32768 float64) the two-pass kernels win, 0.18 vs 0.30 ms
   const int64_t lane_groups = (a.L + 32 * VL - 1) / (32 * VL) * a.O;
-  if (wide && lane_groups >= 64 && (f32 ? launch_softmax_pipe<float>(ctx, a, s) : launch_softmax_pipe<double>(ctx, a, s)))
-    st = ACD_OK;
-  else if (wide && lane_groups >= 64)
+  if (wide && lane_groups >= 64)
     st = f32 ? launch_softmax_l2<float>(ctx, a, s) : launch_softmax_l2<double>(ctx, a, s);
   else if (wide)
     st = f32 ? launch_softmax_wide<float>(ctx, a, s) : launch_softmax_wide<double>(ctx, a, s);
