@@ -24,6 +24,7 @@
 #include "common.cuh"
 #include "ops.cuh"
 #include "reduce_acc.cuh"
+#include "tma.cuh"
 
 namespace acd {
 
@@ -1352,8 +1353,41 @@ acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const a
   if (n == 0) return fail(ACD_ERR_UNSUPPORTED, "acd_permute_fused_stats_keys: empty input");
   if (index_base < 0 || index_base + in->shape[0] > 0xFFFFFFFFLL)
     return fail(ACD_ERR_INVALID, "acd_permute_fused_stats_keys: global index must fit in 32 bits");
-  // the copy (TMA transpose for a permuted matrix), then the chain with its
-  // statistics and keys in one pass over the copy
+  // a transpose (y contiguous along axis 0, in contiguous along another
+  // axis of the collapsed space) runs as one kernel that reads `in` once
+  IterSpace it;
+  it.ndim = y->ndim;
+  it.nops = 2;
+  for (int d = 0; d < y->ndim; ++d) {
+    it.shape[d] = y->shape[d];
+    it.stride[0][d] = y->stride[d];
+    it.stride[1][d] = in->stride[d];
+  }
+  collapse(it);
+  if ((it.ndim == 2 || it.ndim == 3) && it.stride[0][0] == 1 && it.shape[0] == y->shape[0]) {
+    int ai = -1;
+    for (int d = 1; d < it.ndim; ++d)
+      if (it.stride[1][d] == 1) ai = d;
+    if (ai > 0) {
+      int64_t n2 = 1, os2 = 0, is2 = 0;
+      if (it.ndim == 3) {
+        const int bd = 3 - ai;
+        n2 = it.shape[bd];
+        os2 = it.stride[0][bd];
+        is2 = it.stride[1][bd];
+      }
+      DeviceGuard g(ctx->device);
+      bool launched = false;
+      ACD_TRY(launch_permute_chain(ctx, reinterpret_cast<float *>(desc_ptr(y)), reinterpret_cast<float *>(desc_ptr(z)),
+                                   reinterpret_cast<const float *>(desc_ptr(in)), it.shape[0], it.shape[ai], n2,
+                                   it.stride[0][ai], os2, it.stride[1][0], is2, (float)p0, stats, n,
+                                   reinterpret_cast<long long *>(keys), index_base,
+                                   static_cast<cudaStream_t>(stream), &launched));
+      if (launched) return ACD_OK;
+    }
+  }
+  // otherwise the copy (TMA transpose for a permuted matrix), then the chain
+  // with its statistics and keys in one pass over the copy
   ACD_TRY(acd_copy(ctx, y, in, stream));
   return acd_fused_stats_keys(ctx, z, y, p0, stats, keys, index_base, stream);
 }

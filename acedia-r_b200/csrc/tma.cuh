@@ -24,6 +24,11 @@ __device__ __forceinline__ void mbar_init_fence() {
   asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
 }
 
+// One plain arrival.
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
+}
+
 // One arrival that also expects `bytes` of TMA transactions in this phase.
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
   asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_addr(bar)), "r"(bytes)
@@ -101,5 +106,18 @@ bool encode_tensor_map_3d(CUtensorMap *map, const void *base, int elem_bytes, co
 // or are too small to gain from it.
 bool launch_transpose_tma4(acd_ctx *ctx, void *out, const void *in, int64_t n0, int64_t n1, int64_t n2,
                            int64_t os1, int64_t os2, int64_t is0, int64_t is2, cudaStream_t stream);
+
+// Host: the strided-views step in one kernel (permute_chain.cu).  y and z
+// take the geometry of launch_transpose_tma4's `out` (both contiguous, the
+// fibers of the argmax along i, n0 elements each), x that of its `in`.
+// Writes y, z = y*p + exp(-(y^2)), the statistics row of z (as
+// acd_stats_partial, n_total elements) and the argmax keys of z along i (as
+// acd_argmax_keys with index_base).  Sets *launched = false, having launched
+// nothing, when the views do not meet TMA's rules; errors only from scratch
+// allocation or the launch.
+acd_status launch_permute_chain(acd_ctx *ctx, float *y, float *z, const float *x, int64_t n0, int64_t n1,
+                                int64_t n2, int64_t os1, int64_t os2, int64_t is0, int64_t is2, float p,
+                                double *stats, int64_t n_total, long long *keys, int64_t index_base,
+                                cudaStream_t stream, bool *launched);
 
 }  // namespace acd

@@ -54,10 +54,6 @@ struct TtArgs {
   Control *control;
 };
 
-__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_addr(bar)) : "memory");
-}
-
 // Bounded wait that also gives up once another role of the CTA has aborted.
 __device__ __forceinline__ bool tt_wait(uint64_t *bar, uint32_t parity, TtShared *sh, const TtArgs &a) {
   if (mbar_try_wait(bar, parity)) return true;

@@ -89,6 +89,64 @@ def test_permute_fused_stats_keys_matches_separate_calls(acd, xshape, base):
     acd.check_device_status()
 
 
+@pytest.mark.parametrize("xshape,perm,base", [((64, 300, 192), [3, 1, 2], 0), ((256, 160, 256), [3, 1, 2], 5),
+                                              ((64, 5, 128), [3, 2, 1], 0), ((68, 7, 200), [3, 2, 1], 11),
+                                              ((64, 2, 64), [3, 1, 2], 0), ((640, 1, 68), [3, 1, 2], 2 ** 31)])
+def test_permute_one_kernel_shapes(acd, xshape, perm, base):
+    """The one-kernel form (the view is a TMA-eligible transpose): sequences
+    of 1 to 4 tiles, more sequences than CTAs, a batch axis between the two
+    transposed ones (fiber keys at a stride), and edges ragged along either
+    transposed axis."""
+    import acediar.sharded as SH
+    rng = np.random.default_rng(sum(xshape) + base)
+    x = (np.round(rng.normal(0, 1, xshape) * 8) / 8).astype(np.float32)
+    xv = acd.permute_view(acd.as_tensor(x, dtype="float"), perm)
+    y, z, stats, keys = SH.permute_chain_stats_keys(xv, 0.5, base)
+    y_ref = acd.contiguous(xv)
+    assert_exact(y.as_array(), y_ref.as_array(), "y")
+    z_ref = acd.fused("scale_add_exp_neg_square", y_ref, p0=0.5)
+    assert_exact(z.as_array(), z_ref.as_array(), "z")
+    keys_ref, _ = SH.argmax_keys(z_ref, 0, base)
+    assert torch.equal(keys.cpu(), keys_ref.cpu()), "keys"
+    zz = z_ref.as_array()
+    _check_stats(stats.cpu().numpy(), SH.stats_partial(z_ref).cpu().numpy(), zz)
+    xt = np.ascontiguousarray(np.transpose(x, [p - 1 for p in perm]))
+    zo = oracle.gauss_chain(xt, 0.5)
+    bound = 2 * np.spacing(np.maximum(np.abs(xt * np.float32(0.5)), np.exp(-(xt * xt)).astype(np.float32))) + \
+        np.spacing(np.abs(zo))
+    assert np.all(np.abs(zz.astype(np.float64) - zo) <= bound), "z vs the oracle"
+    # the argmax rule of the oracle (first of equal values) on this z
+    idx = SH.decode_keys(keys, zz.shape[1:], one_based=True, dtype="int64").as_array()
+    assert_exact(idx, oracle.arg_reduce("argmax", zz, axis=0, one_based=True) + base, "decoded argmax vs the oracle")
+    acd.check_device_status()
+
+
+def test_permute_one_kernel_infinities_nan_and_signed_zeros(acd):
+    """The one-kernel form with fibers all -inf, all NaN, NaN among values,
+    +inf, and -0/+0 ties (both map to z = 1; the smaller index wins), keys
+    identical to acd_argmax_keys on the separately computed z."""
+    import acediar.sharded as SH
+    x = np.random.default_rng(8).normal(size=(64, 4, 256)).astype(np.float32)
+    x[3, 0, :] = -np.inf
+    x[4, 0, :] = np.nan
+    x[5, 1, 17] = np.nan
+    x[6, 1, 100] = np.inf
+    x[7, 2, :] = 5.0
+    x[7, 2, 90] = -0.0
+    x[7, 2, 30] = 0.0
+    x[8, 3, :] = 5.0
+    x[8, 3, 200] = 0.0
+    x[8, 3, 10] = -0.0
+    xv = acd.permute_view(acd.as_tensor(x, dtype="float"), [3, 1, 2])
+    y, z, stats, keys = SH.permute_chain_stats_keys(xv, 0.5, 3)
+    z_ref = acd.fused("scale_add_exp_neg_square", acd.contiguous(xv), p0=0.5)
+    np.testing.assert_array_equal(z.as_array(), z_ref.as_array())
+    keys_ref, _ = SH.argmax_keys(z_ref, 0, 3)
+    assert torch.equal(keys.cpu(), keys_ref.cpu()), (keys.cpu(), keys_ref.cpu())
+    assert np.isnan(stats.cpu().numpy()[2]) and np.isnan(SH.stats_partial(z_ref).cpu().numpy()[2])
+    acd.check_device_status()
+
+
 def test_fused_stats_keys_infinities_and_nan(acd):
     """Fibers that are all -inf (the first element wins, as in the argmax
     reduction), a fiber with NaN (NaN never wins; the moments turn NaN, as in
