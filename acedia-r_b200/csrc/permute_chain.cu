@@ -53,6 +53,14 @@ constexpr int kPG = 2;                    // compute groups of 8 warps
 constexpr int kPCompute = 256 * kPG;      // compute threads
 constexpr int kPThreads = kPCompute + 64; // plus a load warp and a store warp
 constexpr uint64_t kPWaitNs = 1000000000ull;
+// Group g takes the tiles k with k % G == g, so with NS and NOB multiples of
+// G every stage and output buffer belongs to one group, whose warps take its
+// tiles in order.  The parity waits rely on that: a waiter is never two
+// phases ahead of its barrier.  (With a stage shared by two groups, a group
+// whose earlier tile landed first could wait on a stage whose previous load
+// is still in flight, and the parity of the phase two back would let it
+// through.)
+static_assert(kPNS % kPG == 0 && kPNOB % kPG == 0, "stages and output buffers must divide among the groups");
 
 struct PcShared {
   uint64_t full[kPNS], empty[kPNS], ofull[kPNOB], ofree[kPNOB];
@@ -77,21 +85,23 @@ struct PcArgs {
   Control *control;
 };
 
+// Bounded waits: one thread (the loading and storing roles) or a whole
+// compute warp with one answer for all its lanes.
 __device__ __forceinline__ bool pc_wait(uint64_t *bar, uint32_t parity, PcShared *sh, Control *c) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*reinterpret_cast<volatile int *>(&sh->abort)) return false;
-    if (global_timer_ns() - t0 > kPWaitNs) {
-      *reinterpret_cast<volatile int *>(&sh->abort) = 1;
-      raise_status(c, 2, (int32_t)blockIdx.x);
-      return false;
-    }
-  }
-  return true;
+  return mbar_wait_thread(bar, parity, &sh->abort, c, 2, kPWaitNs);
+}
+__device__ __forceinline__ bool pc_wait_warp(uint64_t *bar, uint32_t parity, PcShared *sh, Control *c) {
+  return mbar_wait_warp(bar, parity, &sh->abort, c, 2, kPWaitNs);
 }
 
-__device__ __forceinline__ void compute_sync() { asm volatile("bar.sync 1, %0;" ::"n"(kPCompute) : "memory"); }
+// Barrier 1 of the compute warps.  The non-aligned form: each thread
+// arrives on its own, so a warp that has not reconverged after the
+// data-dependent branches before it still counts correctly; the __syncwarp
+// reconverges it first all the same.
+__device__ __forceinline__ void compute_sync() {
+  __syncwarp();
+  asm volatile("barrier.sync 1, %0;" ::"n"(kPCompute) : "memory");
+}
 
 // Sequence r of this CTA: its global number s, first column j0 and batch b.
 __device__ __forceinline__ int64_t pc_seq(const PcArgs &a, int64_t r, int &j0, int &b) {
@@ -102,9 +112,9 @@ __device__ __forceinline__ int64_t pc_seq(const PcArgs &a, int64_t r, int &j0, i
   return s;
 }
 
-__device__ __forceinline__ int pc_i0(const PcArgs &a, int64_t s, int64_t t) {
-  return (int)(((t + s) % a.tiles0) * kPT);
-}
+// The i-tile of tile t of sequence s: (t + s) mod tiles0.  Each role takes
+// it once per sequence and then steps it, wrapping, without a division.
+__device__ __forceinline__ int pc_ti(const PcArgs &a, int64_t s, int64_t t) { return (int)((t + s) % a.tiles0); }
 
 __device__ __forceinline__ uint32_t comp(const uint4 &v, int q) {
   return q == 0 ? v.x : (q == 1 ? v.y : (q == 2 ? v.z : v.w));
@@ -143,24 +153,29 @@ __global__ void __launch_bounds__(kPThreads, 1)
   if (warp == kPCompute / 32) {  // loader
     if (lane == 0) {
       int64_t k = 0;
-      for (; k < my_n; ++k) {
-        const int s = (int)(k % kPNS);
-        if (!pc_wait(&sh->empty[s], (uint32_t)(((k / kPNS) & 1) ^ 1), sh, a.control)) break;
-        const int64_t r = k / T;
+      bool go = true;
+      for (int64_t r = 0; go && r < my_nseq; ++r) {
         int j0, b;
         const int64_t sq = pc_seq(a, r, j0, b);
-        const int i0 = pc_i0(a, sq, k - r * T);
         const bool two = j0 + 32 < a.n1;  // a box wholly past the last column is not loaded
-        mbar_arrive_expect_tx(&sh->full[s], two ? kPTile : kPBox);
-        tma_load_3d(sin + s * kPTile, &map_x, &sh->full[s], j0, i0, b);
-        if (two) tma_load_3d(sin + s * kPTile + kPBox, &map_x, &sh->full[s], j0 + 32, i0, b);
+        int ti = pc_ti(a, sq, 0);
+        for (int64_t t = 0; t < T; ++t, ++k) {
+          const int s = (int)(k % kPNS);
+          if (!pc_wait(&sh->empty[s], (uint32_t)(((k / kPNS) & 1) ^ 1), sh, a.control)) {
+            go = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&sh->full[s], two ? kPTile : kPBox);
+          tma_load_3d(sin + s * kPTile, &map_x, &sh->full[s], j0, ti * kPT, b);
+          if (two) tma_load_3d(sin + s * kPTile + kPBox, &map_x, &sh->full[s], j0 + 32, ti * kPT, b);
+          if (++ti == (int)T) ti = 0;
+        }
       }
       if (*reinterpret_cast<volatile int *>(&sh->abort)) {
         // the loads issued last may still be landing in this CTA's shared memory
         for (int64_t q = (k > kPNS ? k - kPNS : 0); q < k; ++q) {
-          const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&sh->full[q % kPNS], (uint32_t)((q / kPNS) & 1)) &&
-                 global_timer_ns() - t0 < kPWaitNs) {
+          WaitClock clk;
+          while (!mbar_try_wait(&sh->full[q % kPNS], (uint32_t)((q / kPNS) & 1)) && !clk.expired(kPWaitNs)) {
           }
         }
       }
@@ -169,24 +184,32 @@ __global__ void __launch_bounds__(kPThreads, 1)
   }
   if (warp == kPCompute / 32 + 1) {  // storer
     if (lane == 0) {
-      for (int64_t k = 0; k < my_n; ++k) {
-        const int ob = (int)(k % kPNOB);
-        if (!pc_wait(&sh->ofull[ob], (uint32_t)((k / kPNOB) & 1), sh, a.control)) break;
-        const int64_t r = k / T;
+      int64_t k = 0;
+      bool go = true;
+      for (int64_t r = 0; go && r < my_nseq; ++r) {
         int j0, b;
         const int64_t sq = pc_seq(a, r, j0, b);
-        const int i0 = pc_i0(a, sq, k - r * T);
-        const unsigned char *ty = sout + ob * 2 * kPTile;
-        tma_store_3d(&map_y, ty, i0, j0, b);
-        tma_store_3d(&map_z, ty + kPTile, i0, j0, b);
-        if (i0 + 32 < a.n0) {
-          tma_store_3d(&map_y, ty + kPBox, i0 + 32, j0, b);
-          tma_store_3d(&map_z, ty + kPTile + kPBox, i0 + 32, j0, b);
-        }
-        bulk_commit();
-        if (k >= 1) {
-          bulk_wait_read<1>();  // the previous tile's stores have read its buffer
-          mbar_arrive(&sh->ofree[(k - 1) % kPNOB]);
+        int ti = pc_ti(a, sq, 0);
+        for (int64_t t = 0; t < T; ++t, ++k) {
+          const int ob = (int)(k % kPNOB);
+          if (!pc_wait(&sh->ofull[ob], (uint32_t)((k / kPNOB) & 1), sh, a.control)) {
+            go = false;
+            break;
+          }
+          const int i0 = ti * kPT;
+          const unsigned char *ty = sout + ob * 2 * kPTile;
+          tma_store_3d(&map_y, ty, i0, j0, b);
+          tma_store_3d(&map_z, ty + kPTile, i0, j0, b);
+          if (i0 + 32 < a.n0) {
+            tma_store_3d(&map_y, ty + kPBox, i0 + 32, j0, b);
+            tma_store_3d(&map_z, ty + kPTile + kPBox, i0 + 32, j0, b);
+          }
+          bulk_commit();
+          if (k >= 1) {
+            bulk_wait_read<1>();  // the previous tile's stores have read its buffer
+            mbar_arrive(&sh->ofree[(k - 1) % kPNOB]);
+          }
+          if (++ti == (int)T) ti = 0;
         }
       }
       bulk_wait_all();
@@ -221,14 +244,17 @@ __global__ void __launch_bounds__(kPThreads, 1)
     // this group's tiles of the sequence: k = r*T + t with k % G == g
     const int64_t k0 = r * T;
     int64_t t = (int64_t)((g - (int)(k0 % kPG) + kPG) % kPG);
+    int ti = pc_ti(a, sq, t);
     for (; live && t < T; t += kPG) {
       const int64_t k = k0 + t;
+      const int i0 = ti * kPT;
+      ti += kPG;
+      while (ti >= (int)T) ti -= (int)T;
       const int s = (int)(k % kPNS);
-      if (!pc_wait(&sh->full[s], (uint32_t)((k / kPNS) & 1), sh, a.control)) {
+      if (!pc_wait_warp(&sh->full[s], (uint32_t)((k / kPNS) & 1), sh, a.control)) {
         live = false;
         break;
       }
-      const int i0 = pc_i0(a, sq, t);
       const unsigned char *tin = sin + s * kPTile + jh * kPBox;
       uint4 rv[4];
 #pragma unroll
@@ -244,7 +270,7 @@ __global__ void __launch_bounds__(kPThreads, 1)
 #pragma unroll
         for (int q = 0; q < 4; ++q) zf[m][q] = f(__uint_as_float(comp(rv[m], q)));
       const int ob = (int)(k % kPNOB);
-      if (!pc_wait(&sh->ofree[ob], (uint32_t)(((k / kPNOB) & 1) ^ 1), sh, a.control)) {
+      if (!pc_wait_warp(&sh->ofree[ob], (uint32_t)(((k / kPNOB) & 1) ^ 1), sh, a.control)) {
         live = false;
         break;
       }
@@ -267,15 +293,21 @@ __global__ void __launch_bounds__(kPThreads, 1)
       const int ibase = i0 + 4 * ib;
       if (jfull && i0 + kPT <= a.n0) {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int q = 0; q < 4; ++q) {
 #pragma unroll
-          for (int m = 0; m < 4; ++m) {
-            const float v = zf[m][q];
-            st.add(v, 0);
-            const bool better = v > av[q] || (v == av[q] && ibase + m < ai[q]);
-            av[q] = better ? v : av[q];
-            ai[q] = better ? ibase + m : ai[q];
+          for (int m = 0; m < 4; ++m) st.add(zf[m][q], 0);
+          // the block's maximum (fmaxf passes NaN over; four NaN give NaN,
+          // which takes no part), then, only when it reaches the running
+          // one, its first position
+          const float tm = fmaxf(fmaxf(zf[0][q], zf[1][q]), fmaxf(zf[2][q], zf[3][q]));
+          if (tm >= av[q]) {
+            const int idx = ibase + (zf[0][q] == tm ? 0 : zf[1][q] == tm ? 1 : zf[2][q] == tm ? 2 : 3);
+            if (tm > av[q] || idx < ai[q]) {
+              av[q] = tm;
+              ai[q] = idx;
+            }
           }
+        }
       } else {  // a ragged tile: elements past either edge take no part
 #pragma unroll
         for (int q = 0; q < 4; ++q) {

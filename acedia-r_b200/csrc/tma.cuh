@@ -45,14 +45,76 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
+// Deadline of a bounded wait.  The clock is %globaltimer; a reading below
+// the start (the timer was set back) restarts the count, and the limit is
+// only declared after at least 4096 polls, so a timer that jumps forward
+// cannot end a short wait.
+struct WaitClock {
+  uint64_t t0 = 0;
+  uint32_t polls = 0;
+  __device__ __forceinline__ bool expired(uint64_t timeout_ns) {
+    const uint64_t now = global_timer_ns();
+    if (polls++ == 0 || now < t0) {
+      t0 = now;
+      return false;
+    }
+    return polls > 4096u && now - t0 > timeout_ns;
+  }
+};
+
 // Waits for the phase with `parity` to complete, at most `timeout_ns`.
 // Returns false when the limit expired.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, uint64_t timeout_ns) {
   if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
+  WaitClock clk;
   while (!mbar_try_wait(bar, parity))
-    if (global_timer_ns() - t0 > timeout_ns) return false;
+    if (clk.expired(timeout_ns)) return false;
   return true;
+}
+
+// Bounded wait of one thread for the phase with `parity`.  Gives up when
+// *abort is set (another role of the CTA gave up) or when the limit expires;
+// then it sets *abort, raises `code` in the context status word and returns
+// false.
+__device__ __forceinline__ bool mbar_wait_thread(uint64_t *bar, uint32_t parity, int *abort, Control *control,
+                                                 int32_t code, uint64_t timeout_ns) {
+  if (mbar_try_wait(bar, parity)) return true;
+  WaitClock clk;
+  while (!mbar_try_wait(bar, parity)) {
+    if (*reinterpret_cast<volatile int *>(abort)) return false;
+    if (clk.expired(timeout_ns)) {
+      *reinterpret_cast<volatile int *>(abort) = 1;
+      raise_status(control, code, (int32_t)blockIdx.x);
+      return false;
+    }
+  }
+  return true;
+}
+
+// The same for a whole warp, with one answer for all its lanes: every lane
+// polls the barrier (each observes the phase, which orders the TMA-written
+// data before its reads), lane 0 alone keeps the clock and reads *abort, and
+// the warp leaves together, so code after the wait never runs with part of
+// the warp.  All 32 lanes must call it.
+__device__ __forceinline__ bool mbar_wait_warp(uint64_t *bar, uint32_t parity, int *abort, Control *control,
+                                               int32_t code, uint64_t timeout_ns) {
+  WaitClock clk;
+  const bool lead = (threadIdx.x & 31) == 0;
+  while (true) {
+    const bool ok = mbar_try_wait(bar, parity);
+    if (__all_sync(0xffffffffu, ok)) return true;
+    int stop = 0;
+    if (lead) {
+      if (*reinterpret_cast<volatile int *>(abort)) {
+        stop = 1;
+      } else if (clk.expired(timeout_ns)) {
+        *reinterpret_cast<volatile int *>(abort) = 1;
+        raise_status(control, code, (int32_t)blockIdx.x);
+        stop = 1;
+      }
+    }
+    if (__shfl_sync(0xffffffffu, stop, 0)) return false;
+  }
 }
 
 // 3-D tiled load of one box into shared memory; completion is counted on `bar`.

@@ -54,19 +54,14 @@ struct TtArgs {
   Control *control;
 };
 
-// Bounded wait that also gives up once another role of the CTA has aborted.
+// Bounded waits that also give up once another role of the CTA has aborted:
+// one thread (the loading and storing roles), or a whole transpose warp with
+// one answer for all its lanes.
 __device__ __forceinline__ bool tt_wait(uint64_t *bar, uint32_t parity, TtShared *sh, const TtArgs &a) {
-  if (mbar_try_wait(bar, parity)) return true;
-  const uint64_t t0 = global_timer_ns();
-  while (!mbar_try_wait(bar, parity)) {
-    if (*reinterpret_cast<volatile int *>(&sh->abort)) return false;
-    if (global_timer_ns() - t0 > kWaitNs) {
-      *reinterpret_cast<volatile int *>(&sh->abort) = 1;
-      raise_status(a.control, 2, (int32_t)blockIdx.x);
-      return false;
-    }
-  }
-  return true;
+  return mbar_wait_thread(bar, parity, &sh->abort, a.control, 2, kWaitNs);
+}
+__device__ __forceinline__ bool tt_wait_warp(uint64_t *bar, uint32_t parity, TtShared *sh, const TtArgs &a) {
+  return mbar_wait_warp(bar, parity, &sh->abort, a.control, 2, kWaitNs);
 }
 
 __device__ __forceinline__ void tt_coords(const TtArgs &a, int64_t k, int &i0, int &j0, int &b) {
@@ -124,9 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       if (*reinterpret_cast<volatile int *>(&sh->abort)) {
         // the loads issued last may still be landing in this CTA's shared memory
         for (int64_t q = (k > kNS ? k - kNS : 0); q < k; ++q) {
-          const uint64_t t0 = global_timer_ns();
-          while (!mbar_try_wait(&sh->full[q % kNS], (uint32_t)((q / kNS) & 1)) &&
-                 global_timer_ns() - t0 < kWaitNs) {
+          WaitClock clk;
+          while (!mbar_try_wait(&sh->full[q % kNS], (uint32_t)((q / kNS) & 1)) && !clk.expired(kWaitNs)) {
           }
         }
       }
@@ -161,7 +155,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int cj = jb & 7, ci = ib & 7;  // 16-byte chunk within a 128-byte row
   for (int64_t k = 0; k < my_n; ++k) {
     const int s = (int)(k % kNS);
-    if (!tt_wait(&sh->full[s], (uint32_t)((k / kNS) & 1), sh, a)) break;
+    if (!tt_wait_warp(&sh->full[s], (uint32_t)((k / kNS) & 1), sh, a)) break;
     const unsigned char *tin = sin + s * kTileBytes + jh * kBoxBytes;
     uint4 r[4];
 #pragma unroll
@@ -172,7 +166,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
     if (lane == 0) mbar_arrive(&sh->empty[s]);
     const int b = (int)(k % kNOB);
-    if (!tt_wait(&sh->ofree[b], (uint32_t)(((k / kNOB) & 1) ^ 1), sh, a)) break;
+    if (!tt_wait_warp(&sh->ofree[b], (uint32_t)(((k / kNOB) & 1) ^ 1), sh, a)) break;
     unsigned char *tout = sout + b * kTileBytes + ih * kBoxBytes;
     const uint4 w0 = make_uint4(r[0].x, r[1].x, r[2].x, r[3].x);
     const uint4 w1 = make_uint4(r[0].y, r[1].y, r[2].y, r[3].y);

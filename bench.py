@@ -3,8 +3,8 @@
 Default workload (the configuration quoted at 1/2/4/8 GPUs): a float32
 256 x 512 x 32768 tensor (2^32 elements, 16 GiB, N(0,1)), sharded along its
 outermost axis, one step =
-    y <- contiguous(permute_view(x, c(3,1,2)))      # transpose kernel
-    z <- y*0.5 + exp(-y^2)                          # one-pass chain kernel, 5 roundings,
+    y <- contiguous(permute_view(x, c(3,1,2)))      # one kernel (acd_permute_fused_stats_keys):
+    z <- y*0.5 + exp(-y^2)                          #   x read once, y and z written once,
     sum(z), var(z)                                  #   with the shard's statistics row
     argmax(z, axis = 1)                             #   and argmax keys
 then one int64 MAX all-reduce of keys and rows (N > 1) and the finish kernel
@@ -33,11 +33,11 @@ N0, N1, N2 = 256, 512, 32768
 CHUNK = 128  # shards hold whole multiples of 128 slices along axis 3
 SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
-BYTES_PER_ELEM = {"transpose": 8, "chain_stats_keys": 8}
-# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 11
-# launches) on the 256x512x1024 case of the same step, scaled by elements to a full launch.  Reads are
-# exactly 4 B/elem; the write side reads low by the ~48 MB of dirty lines still in L2 when a launch ends.
-TRAFFIC_BYTES_PER_ELEM = {"transpose": 7.601, "chain_stats_keys": 7.645}
+# algorithmic bytes per element of the step kernel: x read, y and z written (4 B each)
+BYTES_PER_ELEM = {"permute_chain_stats_keys": 12}
+# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum) on the
+# 256x512x1024 case of the same step, scaled by elements to a full launch
+TRAFFIC_BYTES_PER_ELEM = {"permute_chain_stats_keys": None}
 
 
 def parse():
@@ -461,7 +461,7 @@ def main():
     # two int64 exchange buffers (steps alternate): the argmax keys, then one
     # statistics row per rank; a single MAX all-reduce carries both
     # (acediar.sharded).  Step k's exchange and finish run on a side stream
-    # under step k+1's transpose; step k+2 reuses the buffer once step k's
+    # under step k+1's kernel; step k+2 reuses the buffer once step k's
     # finish has read it.
     nkeys = N0 * N1
     xbufs = [SH.exchange_buffer(nkeys, world, dev) for _ in range(2)]
@@ -478,15 +478,14 @@ def main():
     def stream():
         return ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
 
-    def k_transpose(s, dx=None):
-        L.check(lib.acd_copy(ctx, pref(d_y), pref(dx if dx is not None else d_xp), s), "copy")
-
-    def k_chain_stats_keys(s, b=0):
-        # z = y*0.5 + exp(-y^2), with this shard's statistics row of z and the
-        # argmax keys of z along axis 1 from the same pass (z is not re-read),
-        # written straight into exchange buffer b
-        L.check(lib.acd_fused_stats_keys(ctx, pref(d_z), pref(d_y), ctypes.c_double(0.5), row_ptrs[b], keys_ptrs[b],
-                                         lo, s), "fused_stats_keys")
+    def k_step(s, b=0, dx=None):
+        # y = contiguous(permute(x)), z = y*0.5 + exp(-y^2), this shard's
+        # statistics row of z and the argmax keys of z along axis 1, in one
+        # kernel that reads x once; the row and keys go straight into
+        # exchange buffer b
+        L.check(lib.acd_permute_fused_stats_keys(ctx, pref(d_y), pref(d_z), pref(dx if dx is not None else d_xp),
+                                                 ctypes.c_double(0.5), row_ptrs[b], keys_ptrs[b], lo, s),
+                "permute_fused_stats_keys")
 
     def exchange(b=0, async_op=False):
         if world > 1:
@@ -500,12 +499,11 @@ def main():
     def step(k, dx=None, input_read=None):
         s = stream()
         b = k % 2
-        k_transpose(s, dx)
-        if input_read is not None:
-            input_read.record()  # the transpose is the only reader of the input
         if finished[b] is not None:
             torch.cuda.current_stream().wait_event(finished[b])  # step k-2's finish has read buffer b
-        k_chain_stats_keys(s, b)
+        k_step(s, b, dx)
+        if input_read is not None:
+            input_read.record()  # the step kernel is the only reader of the input
         work = exchange(b, async_op=True)
         side.wait_stream(torch.cuda.current_stream())
         with torch.cuda.stream(side):
@@ -519,7 +517,7 @@ def main():
     def join():
         torch.cuda.current_stream().wait_stream(side)
 
-    LAUNCHES_PER_STEP = 3  # transpose, chain with statistics and keys, exchange finish
+    LAUNCHES_PER_STEP = 2  # the step kernel, the exchange finish
 
     def barrier():
         torch.cuda.synchronize()
@@ -554,21 +552,19 @@ def main():
     # ---- phase split of the step (CUDA events on the launching stream; the
     # synchronous all-reduce makes that stream wait for NCCL's), max over ranks
     PH = 5
-    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(5)] for _ in range(PH)]
+    pev = [[torch.cuda.Event(enable_timing=True) for _ in range(4)] for _ in range(PH)]
     barrier()
     for k in range(PH):
         pev[k][0].record()
-        k_transpose(stream())
+        k_step(stream())
         pev[k][1].record()
-        k_chain_stats_keys(stream())
-        pev[k][2].record()
         exchange()
-        pev[k][3].record()
+        pev[k][2].record()
         k_finish(stream())
-        pev[k][4].record()
+        pev[k][3].record()
     barrier()
-    names = ["transpose", "chain_stats_keys", "exchange", "finish"]
-    ph = torch.tensor([sum(pev[k][j].elapsed_time(pev[k][j + 1]) for k in range(PH)) / PH for j in range(4)],
+    names = ["permute_chain_stats_keys", "exchange", "finish"]
+    ph = torch.tensor([sum(pev[k][j].elapsed_time(pev[k][j + 1]) for k in range(PH)) / PH for j in range(3)],
                       dtype=torch.float64, device=dev)
     if world > 1:
         dist.all_reduce(ph, op=dist.ReduceOp.MAX)
@@ -578,7 +574,7 @@ def main():
 
     # ---- per-kernel durations (CUDA events on the launching stream)
     kern = {}
-    for name, fn in [("transpose", k_transpose), ("chain_stats_keys", k_chain_stats_keys)]:
+    for name, fn in [("permute_chain_stats_keys", k_step)]:
         for _ in range(2):
             fn(stream())
         ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
@@ -594,15 +590,16 @@ def main():
     for name, kms in kern.items():
         byts = BYTES_PER_ELEM[name] * nloc
         gbs = byts / (kms * 1e-3) / 1e9
+        tr = TRAFFIC_BYTES_PER_ELEM[name]
         ops.append({"kernel": name, "ms": round(kms, 4), "bytes": byts, "GB/s": round(gbs, 1),
-                    "frac": round(gbs / peak, 4), "traffic": int(TRAFFIC_BYTES_PER_ELEM[name] * nloc)})
+                    "frac": round(gbs / peak, 4), "traffic": int(tr * nloc) if tr else None})
     top = max(ops, key=lambda o: o["ms"])
 
     # ---- end to end: host buffers in, results out, through the same C ABI.
     # Every step copies its input from pinned host memory and reads its results
     # back.  Two device input buffers let the copy of step k+1 (on a copy
     # stream) run under the kernels of step k: the copy into a buffer waits
-    # for the transpose that last read it, the step waits for its copy.
+    # for the step kernel that last read it, the step waits for its copy.
     e2e = None
     if a.e2e_steps > 0:
         xh = torch.empty(nloc, dtype=torch.float32, pin_memory=True)
