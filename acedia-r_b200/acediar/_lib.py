@@ -111,6 +111,7 @@ def _bind(lib):
         "acd_shard_finish": ([vp, vp, i64, i32, dp, vp, i32, vp], i32),
         "acd_fused_stats_keys": ([vp, dp, dp, f64, vp, vp, i64, vp], i32),
         "acd_permute_fused_stats_keys": ([vp, dp, dp, dp, f64, vp, vp, i64, vp], i32),
+        "acd_copy_fanout": ([vp, vp, vp, vp, i64, vp], i32),
         "acd_selftest_fastdiv": ([u32, u32, P(u32)], i32),
         "acd_selftest_collapse": ([dp, dp, P(i64), P(i64), P(i64)], i32),
     }

@@ -14,8 +14,9 @@ other ranks:
     picks the largest value and, among equal values, the smallest index — the
     reference's first-index rule (src/kernels/tensor_kernels.cu:794).
 The statistics row and the keys can come from the pass that writes the
-elementwise chain (chain_stats_keys; permute_chain_stats_keys adds the
-contiguous copy in front), so z is written once and not re-read.
+elementwise chain (chain_stats_keys), so z is written once and not re-read;
+permute_chain_stats_keys does the whole step, the contiguous copy included,
+in one kernel that reads x once.
 
 Both exchanges travel in one int64 MAX all-reduce over an exchange buffer
 (exchange_buffer, shard_finish): the keys, then one row of six float64 bit
@@ -148,8 +149,10 @@ def chain_stats_keys(y, p0, index_base):
 
 def permute_chain_stats_keys(x, p0, index_base):
     """y = contiguous(x) of the permuted view x, then z = y*p0 + exp(-(y^2)),
-    the statistics row of z and its argmax keys along axis 1 from one pass
-    over y: the strided-views step in one call (two kernels)."""
+    the statistics row of z and its argmax keys along axis 1: the
+    strided-views step in one call.  When x is a transpose TMA can read (the
+    usual case) this is one kernel that reads x once; otherwise the copy and
+    then the one-pass chain."""
     y = _alloc(x.shape, x.dtype, x.device)
     z = _alloc(x.shape, x.dtype, x.device)
     stats = torch.empty(STATS_WIDTH, dtype=torch.float64, device=x.device)

@@ -693,6 +693,31 @@ static acd_status convert_from(acd_ctx *ctx, const acd_desc *out, const acd_desc
 
 using namespace acd;
 
+// Contiguous copy into one or two destinations (16-byte vectors, four in
+// flight per thread): the streaming rate of one read against one or two
+// writes, the ceiling of a kernel with that traffic mix.
+template <bool TWO>
+__global__ void __launch_bounds__(256) k_fanout(const uint4 *__restrict__ src, uint4 *__restrict__ d0,
+                                               uint4 *__restrict__ d1, int64_t n) {
+  const int64_t nth = (int64_t)gridDim.x * blockDim.x;
+  int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  for (; i + 3 * nth < n; i += 4 * nth) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) v[u] = src[i + u * nth];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      d0[i + u * nth] = v[u];
+      if (TWO) d1[i + u * nth] = v[u];
+    }
+  }
+  for (; i < n; i += nth) {
+    const uint4 v = src[i];
+    d0[i] = v;
+    if (TWO) d1[i] = v;
+  }
+}
+
 extern "C" {
 
 acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream) {
@@ -926,6 +951,28 @@ acd_status acd_fused(acd_ctx *ctx, int32_t op, const acd_desc *out, const acd_de
     return fail(ACD_ERR_INVALID, "acd_fused: bad op %d", op);
   }
   if (st != ACD_OK) return st;
+  ACD_CUDA(cudaGetLastError());
+  return ACD_OK;
+}
+
+acd_status acd_copy_fanout(acd_ctx *ctx, void *dst0, void *dst1, const void *src, int64_t nbytes,
+                           acd_stream stream) {
+  if (!ctx || !dst0 || !src) return fail(ACD_ERR_INVALID, "acd_copy_fanout: null argument");
+  if (nbytes < 0 || nbytes % 16 ||
+      ((reinterpret_cast<uintptr_t>(dst0) | reinterpret_cast<uintptr_t>(dst1) | reinterpret_cast<uintptr_t>(src)) & 15))
+    return fail(ACD_ERR_INVALID, "acd_copy_fanout: 16-byte aligned buffers and a multiple of 16 bytes required");
+  if (nbytes == 0) return ACD_OK;
+  DeviceGuard g(ctx->device);
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  const int64_t n = nbytes / 16;
+  const uint4 *ps = static_cast<const uint4 *>(src);
+  if (dst1) {
+    const int grid = persistent_grid(ctx, k_fanout<true>, 256, 0, (n + 1023) / 1024);
+    k_fanout<true><<<grid, 256, 0, s>>>(ps, static_cast<uint4 *>(dst0), static_cast<uint4 *>(dst1), n);
+  } else {
+    const int grid = persistent_grid(ctx, k_fanout<false>, 256, 0, (n + 1023) / 1024);
+    k_fanout<false><<<grid, 256, 0, s>>>(ps, static_cast<uint4 *>(dst0), nullptr, n);
+  }
   ACD_CUDA(cudaGetLastError());
   return ACD_OK;
 }

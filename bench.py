@@ -35,9 +35,10 @@ SEED = 42
 CPU_SAMPLE_N2 = 2048  # CPU baseline sample: 256 x 512 x 2048 (2^28 elements)
 # algorithmic bytes per element of the step kernel: x read, y and z written (4 B each)
 BYTES_PER_ELEM = {"permute_chain_stats_keys": 12}
-# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum) on the
-# 256x512x1024 case of the same step, scaled by elements to a full launch
-TRAFFIC_BYTES_PER_ELEM = {"permute_chain_stats_keys": None}
+# DRAM bytes per element that ncu measured (dram__bytes_read.sum + dram__bytes_write.sum, mean of 10
+# launches) on the 256x512x1024 case of the same step, scaled by elements to a full launch.  Reads are
+# exactly 4 B/elem; the write side reads low by the ~58 MB of dirty lines still in L2 when a launch ends.
+TRAFFIC_BYTES_PER_ELEM = {"permute_chain_stats_keys": 11.568}
 
 
 def parse():
@@ -585,6 +586,21 @@ def main():
         ev[1].record()
         torch.cuda.synchronize()
         kern[name] = ev[0].elapsed_time(ev[1]) / reps
+    # ---- the ceiling of the step's traffic mix: x read once, written to y and
+    # to z, as plain contiguous streaming (no transpose, no arithmetic)
+    def k_fanout(s):
+        L.check(lib.acd_copy_fanout(ctx, ctypes.c_void_p(y.storage.data_ptr()), ctypes.c_void_p(z.storage.data_ptr()),
+                                    ctypes.c_void_p(x.storage.data_ptr()), nloc * 4, s), "copy_fanout")
+
+    for _ in range(2):
+        k_fanout(stream())
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(2)]
+    ev[0].record()
+    for _ in range(5):
+        k_fanout(stream())
+    ev[1].record()
+    torch.cuda.synchronize()
+    fan_gbs = 12 * nloc / (ev[0].elapsed_time(ev[1]) / 5 * 1e-3) / 1e9
     peak, peak_kind = peaks()
     ops = []
     for name, kms in kern.items():
@@ -678,7 +694,10 @@ def main():
             "roofline": {"bound": "hbm", "achieved": top["GB/s"], "peak": peak, "unit": "GB/s",
                          "frac": round(top["GB/s"] / peak, 4), "traffic": top["traffic"], "kernel": top["kernel"],
                          "peak_source": peak_kind, "traffic_source": "ncu dram bytes/elem of the 256x512x1024 "
-                         "case x elements per launch"},
+                         "case x elements per launch",
+                         "mix_ceiling": {"what": "acd_copy_fanout: the same bytes read once and written twice, "
+                                         "contiguous streaming, this run", "GB/s": round(fan_gbs, 1),
+                                         "frac": round(top["GB/s"] / fan_gbs, 4)}},
             "ops": ops,
             "phases_ms": phases,
             "gpu_launches": LAUNCHES_PER_STEP * a.steps,

@@ -256,6 +256,12 @@ acd_status acd_convert(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, ac
 
 /* out = in, any strides on both sides (contiguous(), strided copy). */
 acd_status acd_copy(acd_ctx *ctx, const acd_desc *out, const acd_desc *in, acd_stream stream);
+/* nbytes of src copied to dst0 and, when dst1 is not NULL, to dst1 too;
+ * 16-byte aligned buffers, nbytes a multiple of 16.  Plain streaming: the
+ * benchmark times it as the ceiling of a kernel that reads once and writes
+ * once or twice (the strided-views step writes y and z for each x). */
+acd_status acd_copy_fanout(acd_ctx *ctx, void *dst0, void *dst1, const void *src, int64_t nbytes,
+                           acd_stream stream);
 
 /* ---- reductions -------------------------------------------------------- */
 /* Reduces the axes whose bit is set in axes_mask (bit k = axis k, 0-based).
@@ -343,8 +349,13 @@ acd_status acd_fused_stats_keys(acd_ctx *ctx, const acd_desc *out, const acd_des
 /* y = contiguous(in) for the view `in`, then z, the statistics row and the
  * argmax keys of acd_fused_stats_keys(z, y, ...): the strided-views step's
  * permute -> contiguous (R/gpuTensor.R:1544-1556, src/gpuTensor.h:723-769),
- * elementwise chain, statistics and argmax keys as one call of two kernels.
- * y and z are contiguous FLOAT32 of in's shape. */
+ * elementwise chain, statistics and argmax keys as one call.  y and z are
+ * contiguous FLOAT32 of in's shape.  When `in` is a transpose of y (y
+ * contiguous along axis 0, `in` contiguous along another axis after
+ * collapsing, 16-byte aligned data and strides, both transposed extents at
+ * least 64) it is one kernel that reads `in` once and writes y and z once;
+ * otherwise the copy and then acd_fused_stats_keys.  Results are identical
+ * either way (y, z and keys bit for bit; the moments to summation order). */
 acd_status acd_permute_fused_stats_keys(acd_ctx *ctx, const acd_desc *y, const acd_desc *z, const acd_desc *in,
                                         double p0, double *stats, int64_t *keys, int64_t index_base,
                                         acd_stream stream);

@@ -5,6 +5,7 @@ correctly rounded), max/min, abs/floor/ceil/round/relu/neg, comparisons and
 every integer op; <= 2 ulp for exp/log/sqrt/tanh/sigmoid/erf/sin/cos/pow.
 """
 import numpy as np
+import torch
 import pytest
 
 import oracle
@@ -192,3 +193,27 @@ def test_copy_permutations_bit_exact(acd, name, dt):
         for perm in itertools.permutations(range(1, len(shape) + 1)):
             got = acd.contiguous(acd.permute_view(t, list(perm))).as_array()
             assert_exact(got, np.transpose(x, [p - 1 for p in perm]), "%s perm %s" % (shape, perm))
+
+
+def test_copy_fanout(acd):
+    """acd_copy_fanout: one source into one or two destinations, bit for bit;
+    misaligned buffers and sizes are refused before any launch."""
+    import ctypes
+    import acediar._lib as L
+    from acediar.tensor import context
+    src = torch.randint(-2 ** 31, 2 ** 31 - 1, (1 << 20,), dtype=torch.int32, device="cuda")
+    d0 = torch.zeros_like(src)
+    d1 = torch.zeros_like(src)
+    s = ctypes.c_void_p(torch.cuda.current_stream().cuda_stream)
+    lib = L.lib()
+    assert lib.acd_copy_fanout(context(), ctypes.c_void_p(d0.data_ptr()), ctypes.c_void_p(d1.data_ptr()),
+                               ctypes.c_void_p(src.data_ptr()), src.numel() * 4, s) == 0
+    assert torch.equal(d0, src) and torch.equal(d1, src)
+    d2 = torch.zeros_like(src)
+    assert lib.acd_copy_fanout(context(), ctypes.c_void_p(d2.data_ptr()), None, ctypes.c_void_p(src.data_ptr()),
+                               4096 * 4, s) == 0
+    assert torch.equal(d2[:4096], src[:4096]) and int(d2[4096:].abs().sum()) == 0
+    assert lib.acd_copy_fanout(context(), ctypes.c_void_p(d2.data_ptr() + 4), None, ctypes.c_void_p(src.data_ptr()),
+                               64, s) != 0
+    assert lib.acd_copy_fanout(context(), ctypes.c_void_p(d2.data_ptr()), None, ctypes.c_void_p(src.data_ptr()),
+                               40, s) != 0
