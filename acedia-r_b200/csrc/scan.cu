@@ -24,8 +24,9 @@
 // neighbouring lanes sit next to each other in memory) take a three-kernel
 // reduce-then-scan instead, which has no waits between CTAs:
 //   1. k_lane_reduce: one warp per (lane block, step segment) task reads its
-//      segment row by row (LT lanes x G step phases per warp, so a warp load
-//      covers G rows of LT lanes) and writes one total per lane;
+//      segment row by row, last row first (LT lanes x G step phases per warp,
+//      so a warp load covers G rows of LT lanes) and writes one total per
+//      lane;
 //   2. k_lane_seg_scan: one CTA per (chain, lane) turns the segment totals
 //      into exclusive prefixes in place;
 //   3. k_lane_apply: the same warps re-read their segments and write
@@ -81,16 +82,24 @@ __global__ void __launch_bounds__(256) k_lane_reduce(LaneArgs a) {
     const LaneTask<LT> k(a, t, li);
     double acc = ident;
     if (k.l < a.L && k.rs + g < k.re) {
+      // the segment is read from its last row back to its first, so the rows
+      // this pass leaves in L2 are the segments' first rows, the ones
+      // k_lane_apply reads first
       int64_t n = (k.re - k.rs - g + G - 1) / G;
-      const T *p = static_cast<const T *>(a.in) + k.o * a.so + k.l * a.sl + (k.rs + g) * a.sr;
-      for (; n >= U; n -= U, p += U * step) {
+      const int64_t last = (k.rs + g + (n - 1) * G) * a.sr;
+      const T *p = static_cast<const T *>(a.in) + k.o * a.so + k.l * a.sl + last;
+      for (; n >= U; n -= U) {
         T v[U];
 #pragma unroll
-        for (int j = 0; j < U; ++j) v[j] = p[j * step];
+        for (int j = 0; j < U; ++j) v[j] = p[-j * step];
 #pragma unroll
         for (int j = 0; j < U; ++j) acc = combine<PROD>(acc, (double)v[j]);
+        if (n > U) p -= U * step;
       }
-      for (; n > 0; --n, p += step) acc = combine<PROD>(acc, (double)*p);
+      for (; n > 0; --n) {
+        acc = combine<PROD>(acc, (double)*p);
+        if (n > 1) p -= step;
+      }
     }
 #pragma unroll
     for (int d = LT; d < 32; d <<= 1) acc = combine<PROD>(acc, __shfl_xor_sync(0xffffffffu, acc, d));

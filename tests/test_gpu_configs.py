@@ -196,10 +196,11 @@ def test_c4_row_softmax(acd):
 
 # ---------------------------------------------------------------------------
 def test_c5_views_step_at_full_size(acd):
-    """The bench step's calls at 2^32 elements against the oracle run slab by
-    slab from the same x: global sum and var (relative 1e-5) and every one of
-    the 256x512 argmax fibers (exact).  The separate R-level ops on z are
-    checked too (sum, var, argmax along axis 1)."""
+    """The bench step's call at 2^32 elements (the one-kernel step) against
+    the oracle run slab by slab from the same x: global sum and var (relative
+    1e-5) and every one of the 256x512 argmax fibers (exact); y and z
+    bit-identical to contiguous() and the fused chain.  The separate R-level
+    ops on z are checked too (sum, var, argmax along axis 1)."""
     import ctypes
 
     import acediar._lib as L
@@ -212,9 +213,15 @@ def test_c5_views_step_at_full_size(acd):
     # as the bench: normal(0, 1) from Philox seed 42, counter = global index
     L.check(L.lib().acd_rand(context(), ctypes.byref(x.desc()), 1, ctypes.c_double(0.0), ctypes.c_double(1.0),
                              ctypes.c_uint64(42), ctypes.c_uint64(0), _stream()), "rand")
-    y = acd.contiguous(acd.permute_view(x, [3, 1, 2]))
-    z, stats, keys = SH.chain_stats_keys(y, 0.5, 0)
-    del y
+    # the bench's step: one kernel (acd_permute_fused_stats_keys)
+    xv = acd.permute_view(x, [3, 1, 2])
+    y, z, stats, keys = SH.permute_chain_stats_keys(xv, 0.5, 0)
+    y_ref = acd.contiguous(xv)
+    assert torch.equal(y.storage[:n], y_ref.storage[:n]), "C5 y = contiguous(permute(x)), bit for bit"
+    del y_ref
+    z_ref = acd.fused("scale_add_exp_neg_square", y, p0=0.5)
+    assert torch.equal(z.storage[:n], z_ref.storage[:n]), "C5 z = y*0.5 + exp(-y^2), bit for bit"
+    del y, z_ref
     tot, var = (float(t.item()) for t in SH.merge_stats_torch(stats.view(1, -1)))
     idx = SH.decode_keys(keys, (n0, n1), one_based=True, dtype="int32").as_array()
     s_op, v_op = acd.sum(z), acd.var(z)
@@ -248,9 +255,9 @@ def test_c5_views_step_at_full_size(acd):
         st.second(zslab(c0))
     ref = st.result()
     ref_idx = (arg + 1).reshape((n0, n1), order="F")
-    assert_rel(tot, ref["sum"], F32, "C5 sum (one-pass chain kernel)")
-    assert_rel(var, ref["var"], F32, "C5 var (one-pass chain kernel)")
-    assert_exact(idx.astype(np.int64), ref_idx, "C5 argmax along axis 1, all 131072 fibers (one-pass keys)")
+    assert_rel(tot, ref["sum"], F32, "C5 sum (step kernel)")
+    assert_rel(var, ref["var"], F32, "C5 var (step kernel)")
+    assert_exact(idx.astype(np.int64), ref_idx, "C5 argmax along axis 1, all 131072 fibers (step kernel keys)")
     assert_rel(s_op, ref["sum"], F32, "C5 sum(z)")
     assert_rel(v_op, ref["var"], F32, "C5 var(z)")
     assert_exact(am_op.astype(np.int64), ref_idx, "C5 argmax(z, axis=1)")
